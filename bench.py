@@ -1,0 +1,466 @@
+"""Benchmark of the 4-bit paged decode hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: launched by torch.distributed.run, one process per GPU)
+
+Workload per GPU (weak scaling): 64 sequences of a global ragged batch of
+64*N sequences with lengths ~ U[128, 8192] (seeded), assigned to ranks by
+longest-first bin packing on token count; Hq=32, Hkv=8, D=128, block_size 16,
+pages randomly permuted in a pool sized to the tokens, int32 block tables,
+K/V ~ N(0,1) fp16 quantized into the pool by the store kernel.  One step =
+append 1 new token per sequence (kv_quantize_store) + ragged decode of every
+sequence (split-K kernel + combine), i.e. one attention layer of one decode
+step.  The pool (~290 MB/GPU) is larger than L2, so no flush is needed.
+
+Reported: tok/s (sequences decoded per second, all GPUs), µs/step, the
+decode kernel's algorithmic HBM GB/s against MEASURED_PEAKS.json, an
+end-to-end figure through the public Python API with pinned host buffers,
+and the CPU oracle timed on this host.  ``--impl reference`` times the
+reference path's CPU restatement (oracle/kvq_oracle.c) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = ("µs/decode-step & achieved HBM GB/s (% of 8 TB/s) for 4-bit paged decode; "
+          "tok/s @1/2/4/8")
+SEQS_PER_GPU = 64
+HQ, HKV, D, BS = 32, 8, 128, 16
+LMIN, LMAX = 128, 8192
+SEED = 1234
+NOMINAL_HBM_GBS = 8000.0
+
+
+# --------------------------------------------------------------------- setup
+def global_lengths(world: int):
+    g = torch.Generator().manual_seed(SEED)
+    return torch.randint(LMIN, LMAX + 1, (SEQS_PER_GPU * world,), generator=g).tolist()
+
+
+def rank_lengths(world: int, rank: int):
+    from slm_turbo_b200.sharding import partition_sequences
+    lengths = global_lengths(world)
+    parts = partition_sequences(lengths, world)
+    return [lengths[i] for i in parts[rank]]
+
+
+def build_workload(lengths, rank: int):
+    """Host tensors of the rank's pool: block tables, slot ids, seeded K/V, q."""
+    g = torch.Generator().manual_seed(SEED + 1000 + rank)
+    L1 = [L + 1 for L in lengths]  # each step appends one token at position L
+    nblk = [(L + BS - 1) // BS for L in L1]
+    total = sum(nblk)
+    perm = torch.randperm(total, generator=g)
+    bt = torch.zeros(len(lengths), max(nblk), dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    return dict(lengths=lengths, seq_lens1=torch.tensor(L1, dtype=torch.int32), block_tables=bt,
+                num_blocks=total, gen=g)
+
+
+def prefill_cache(w, dev):
+    """Quantize N(0,1) history tokens into the permuted pool (chunked)."""
+    from slm_turbo_b200.kernels import kv_dequant as kd
+    cache = torch.zeros(w["num_blocks"], BS, HKV, D + 8, dtype=torch.uint8, device=dev)
+    bt = w["block_tables"].to(torch.int64)
+    g = torch.Generator(device=dev).manual_seed(SEED + 7)
+    for i, L in enumerate(w["lengths"]):
+        t = torch.arange(L)
+        slots = (bt[i, t // BS] * BS + t % BS).to(dev)
+        k = torch.randn(L, HKV, D, device=dev, generator=g, dtype=torch.float32).half()
+        v = torch.randn(L, HKV, D, device=dev, generator=g, dtype=torch.float32).half()
+        kd.kv_quantize_store(k, v, cache, slots, BS)
+    torch.cuda.synchronize(dev)
+    return cache
+
+
+def step_slots(w):
+    bt = w["block_tables"].to(torch.int64)
+    pos = torch.tensor(w["lengths"], dtype=torch.int64)
+    return bt[torch.arange(len(w["lengths"])), pos // BS] * BS + pos % BS
+
+
+def algorithmic_bytes(w):
+    """Bytes the decode kernel must move (SURVEY 8(d) C3 formula): packed slots
+    of every context token and kv head, block-table entries, q in, out (fp32)."""
+    toks = int(w["seq_lens1"].sum())
+    pages = sum((L + BS - 1) // BS for L in w["seq_lens1"].tolist())
+    B = len(w["lengths"])
+    decode = toks * HKV * (D + 8) + pages * 4 + B * HQ * D * (2 + 4) + B * 4
+    store = B * HKV * D * 2 * 2 + B * HKV * (D + 8) + B * 8
+    return decode, store
+
+
+# -------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML during the timed region."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                r = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons)}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ profiles
+def profiled_traffic():
+    """dram read+write bytes per decode launch from the committed ncu summary
+    (a `traffic_bytes_per_launch:` line), or None."""
+    p = ROOT / "profiles" / "decode_splitk_c3.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def measured_peak():
+    try:
+        mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(mp["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    except Exception:
+        return 6650.0, "profiling-recipe fallback 6.65 TB/s (of fallback)"
+
+
+# ---------------------------------------------------------------- CPU legs
+def cpu_step_time(w_host, cache_np, reps_seconds=10.0, max_reps=50):
+    """Time the oracle on this host: store of the step's tokens + decode of
+    every sequence (all host threads).  Returns (seconds per step, reps, threads)."""
+    import oracle
+    B = len(w_host["lengths"])
+    g = torch.Generator().manual_seed(99)
+    q = torch.randn(B, HQ, D, generator=g).half()
+    k = torch.randn(B, HKV, D, generator=g).half()
+    v = torch.randn(B, HKV, D, generator=g).half()
+    slots = step_slots(w_host)
+    nthreads = os.cpu_count() or 1
+    times = []
+    t_all = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        oracle.kv_store(k, v, cache_np, slots)
+        oracle.paged_decode(q, cache_np, w_host["block_tables"], w_host["seq_lens1"], BS, HKV,
+                            nthreads=nthreads)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > reps_seconds or len(times) >= max_reps:
+            break
+    return statistics.median(times), len(times), nthreads
+
+
+def cpu_cache_for(w_host):
+    """Fill a host pool with the oracle store (the CPU path's own setup)."""
+    import oracle
+    cache = np.zeros((w_host["num_blocks"], BS, HKV, D + 8), np.uint8)
+    bt = w_host["block_tables"].to(torch.int64)
+    g = torch.Generator().manual_seed(SEED + 7)
+    for i, L in enumerate(w_host["lengths"]):
+        t = torch.arange(L)
+        slots = bt[i, t // BS] * BS + t % BS
+        k = torch.randn(L, HKV, D, generator=g).half()
+        v = torch.randn(L, HKV, D, generator=g).half()
+        oracle.kv_store(k, v, cache, slots)
+    return cache
+
+
+# --------------------------------------------------------------------- main
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def workload_config(w, world):
+    toks = int(w["seq_lens1"].sum())
+    return {"workload": "C3 ragged paged 4-bit decode: per GPU 64 seqs U[128,8192] (+1 appended token/step), "
+                        "Hq32/Hkv8/D128, block 16, permuted page pool, int32 block tables",
+            "seqs_per_gpu": len(w["lengths"]), "global_seqs": SEQS_PER_GPU * world,
+            "ctx_tokens_rank0": toks, "pool_mb_rank0": round(w["num_blocks"] * BS * HKV * (D + 8) / 1e6, 1),
+            "l2": "inputs larger than L2 (page pool > 126 MB), no flush",
+            "parallelism": f"seq-partition x{world} (no collective)"}
+
+
+def run_reference(args):
+    """CPU restatement of the reference path (oracle/kvq_oracle.c, all host
+    threads) on rank 0's workload.  Each step is a bounded sample: a fixed
+    subset of the sequences sized so the K+W steps take ~2 minutes at most;
+    time is scaled to the full workload by context tokens."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import oracle
+    lengths = rank_lengths(world, 0)
+    w = build_workload(lengths, 0)
+    cache_np = cpu_cache_for(w)
+    B = len(lengths)
+    g = torch.Generator().manual_seed(99)
+    q = torch.randn(B, HQ, D, generator=g).half()
+    k = torch.randn(B, HKV, D, generator=g).half()
+    v = torch.randn(B, HKV, D, generator=g).half()
+    slots = step_slots(w)
+    nthreads = os.cpu_count() or 1
+
+    def one(idx):
+        oracle.kv_store(k[idx], v[idx], cache_np, slots[idx])
+        oracle.paged_decode(q[idx], cache_np, w["block_tables"][idx], w["seq_lens1"][idx], BS, HKV,
+                            nthreads=nthreads)
+
+    full = torch.arange(B)
+    t0 = time.perf_counter()
+    one(full)
+    t_full = time.perf_counter() - t0
+    budget = 100.0 / max(args.steps + args.warmup, 1)
+    n = B if t_full <= budget else max(1, int(B * budget / t_full))
+    idx = torch.randperm(B, generator=torch.Generator().manual_seed(5))[:n].sort().values
+    toks_all = float(w["seq_lens1"].sum())
+    toks_s = float(w["seq_lens1"][idx].sum())
+    for _ in range(args.warmup):
+        one(idx)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one(idx)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1) * (toks_all / toks_s)
+    value = B / dt
+    sample = (f"{n} of {B} rank-0 sequences per step ({int(toks_s)} of {int(toks_all)} context tokens), "
+              f"time scaled by tokens; oracle/kvq_oracle.c, OpenMP {nthreads} threads, f64 attention")
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": workload_config(w, world),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": nthreads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        args.gpus = world
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    from slm_turbo_b200.kernels import kv_dequant as kd
+
+    lengths = rank_lengths(world, rank)
+    w = build_workload(lengths, rank)
+    cache = prefill_cache(w, dev)
+    B = len(lengths)
+    bt_d = w["block_tables"].to(dev)
+    sl_d = w["seq_lens1"].to(dev)
+    slots_d = step_slots(w).to(dev)
+    g = torch.Generator(device=dev).manual_seed(SEED + 11 + rank)
+    q = torch.randn(B, HQ, D, device=dev, generator=g).half()
+    k_new = torch.randn(B, HKV, D, device=dev, generator=g).half()
+    v_new = torch.randn(B, HKV, D, device=dev, generator=g).half()
+    out = torch.empty(B, HQ, D, dtype=torch.float32, device=dev)
+    maxlen = int(w["seq_lens1"].max())
+
+    def step():
+        kd.kv_quantize_store(k_new, v_new, cache, slots_d, BS)
+        kd.kv_decode_paged_batched(q, cache, bt_d, sl_d, out=out, max_seq_len=maxlen)
+
+    def decode_only():
+        kd.kv_decode_paged_batched(q, cache, bt_d, sl_d, out=out, max_seq_len=maxlen)
+
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    def max_over_ranks(x):
+        if pg is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up, then K timed steps (device-timed, max over ranks) ----
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    assert kd.read_device_errors(dev) == 0, "device error word set during warm-up"
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+
+    # ---- dominant kernel: decode op alone (split-K + combine), per launch ----
+    n_dec = max(args.steps, 20)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_dec)]
+    for a, b in evs:
+        a.record(stream)
+        decode_only()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    dec_ms = max_over_ranks(dec_ms)
+    dec_bytes, store_bytes = algorithmic_bytes(w)
+    peak, peak_src = measured_peak()
+    achieved = dec_bytes / (dec_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public API with pinned host buffers ----
+    h_q = q.cpu().pin_memory()
+    h_k = k_new.cpu().pin_memory()
+    h_v = v_new.cpu().pin_memory()
+    h_slots = step_slots(w).pin_memory()
+    h_sl = w["seq_lens1"].pin_memory()
+    h_out = torch.empty(B, HQ, D, dtype=torch.float32).pin_memory()
+    d_q, d_k, d_v = torch.empty_like(q), torch.empty_like(k_new), torch.empty_like(v_new)
+    d_slots, d_sl = torch.empty_like(slots_d), torch.empty_like(sl_d)
+
+    def e2e_step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_k.copy_(h_k, non_blocking=True)
+        d_v.copy_(h_v, non_blocking=True)
+        d_slots.copy_(h_slots, non_blocking=True)
+        d_sl.copy_(h_sl, non_blocking=True)
+        kd.kv_quantize_store(d_k, d_v, cache, d_slots, BS)
+        kd.kv_decode_paged_batched(d_q, cache, bt_d, d_sl, out=out, max_seq_len=maxlen)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_sl))
+    d2h = h_out.numel() * h_out.element_size()
+    assert kd.read_device_errors(dev) == 0, "device error word set during timing"
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cache_np = cpu_cache_for(w)
+        t_cpu, reps, nthreads = cpu_step_time(w, cache_np, reps_seconds=args.cpu_seconds)
+        cpu = {"value": B / t_cpu, "unit": "tok/s", "cores": nthreads, "kind": "port",
+               "sample": f"full rank-0 workload ({B} seqs, store + decode), median of {reps} steps, "
+                         f"oracle/kvq_oracle.c (OpenMP, f64 attention)"}
+
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    total_seqs = SEQS_PER_GPU * world  # every sequence of the global batch decodes once per step
+    tok_s = total_seqs / (ms_step * 1e-3)
+    line = {
+        "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": workload_config(w, world),
+        "decode_us": dec_ms * 1e3, "decode_hbm_gbs": achieved,
+        "hbm_pct_of_8tbs": 100.0 * achieved / NOMINAL_HBM_GBS,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": profiled_traffic(),
+                     "kernel": "decode_splitk_kernel<128,1,PAGED> + decode_combine_kernel (timed together)",
+                     "algorithmic_bytes_per_launch": dec_bytes, "peak_source": peak_src},
+        "e2e": {"value": total_seqs / (e2e_ms * 1e-3),
+                "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,440 @@
+// decode.cu -- host launchers (C ABI) of the split-K decode kernels.
+#include <mutex>
+
+#include "decode_kernels.cuh"
+#include "internal.h"
+
+namespace slmt {
+
+namespace {
+
+constexpr int kMaxCtasPerSm = 4;       // cap used by the workspace bound
+constexpr int kMinTilesPerCta = 4;     // do not split below ~64 tokens per CTA
+constexpr int kSmemPerSm = 233472;     // 228 KB shared memory per SM (sm_100)
+constexpr int kSmemPerCtaMax = 232448; // 227 KB opt-in per CTA
+constexpr int kSmemReserved = 1024;    // reserved per resident CTA
+
+inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+using DecodeFn = void (*)(const DecodeParams);
+using CombineFn = void (*)(const DecodeParams, void*, int, int64_t, int64_t);
+
+template <int D, int NT>
+DecodeFn decode_fn_layout(int layout) {
+  switch (layout) {
+    case LAYOUT_PAGED:
+      return decode_splitk_kernel<D, NT, LAYOUT_PAGED>;
+    case LAYOUT_PER_CHANNEL:
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL>;
+    default:
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN>;
+  }
+}
+
+DecodeFn decode_fn(int D, int nt, int layout) {
+  if (D == 64) return nt == 1 ? decode_fn_layout<64, 1>(layout) : decode_fn_layout<64, 2>(layout);
+  if (D == 80) return nt == 1 ? decode_fn_layout<80, 1>(layout) : decode_fn_layout<80, 2>(layout);
+  return nt == 1 ? decode_fn_layout<128, 1>(layout) : decode_fn_layout<128, 2>(layout);
+}
+
+CombineFn combine_fn(int D) {
+  if (D == 64) return decode_combine_kernel<64>;
+  if (D == 80) return decode_combine_kernel<80>;
+  return decode_combine_kernel<128>;
+}
+
+struct OccEntry {
+  int device;
+  const void* fn;
+  int smem;
+  int occ;
+};
+
+std::mutex g_occ_mu;
+OccEntry g_occ[256];
+int g_occ_n = 0;
+
+// Resident CTAs per SM for `fn` at `smem` bytes (opts the kernel into large
+// dynamic shared memory the first time it is seen on a device).
+int occupancy(int device, const void* fn, int smem) {
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  for (int i = 0; i < g_occ_n; ++i)
+    if (g_occ[i].device == device && g_occ[i].fn == fn && g_occ[i].smem == smem) return g_occ[i].occ;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemPerCtaMax) !=
+      cudaSuccess)
+    return -1;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, smem) != cudaSuccess) return -1;
+  if (g_occ_n < 256) g_occ[g_occ_n++] = OccEntry{device, fn, smem, occ};
+  return occ;
+}
+
+std::mutex g_sm_mu;
+int g_sms[64] = {0};
+
+}  // namespace
+
+int current_device_sms(int* device_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (device_out) *device_out = dev;
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lk(g_sm_mu);
+    if (g_sms[dev] > 0) return g_sms[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    g_sms[dev] = n;
+    return n;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  return n;
+}
+
+namespace {
+
+struct Geometry {
+  int G, nt, kvc, ngroups, wpk;
+};
+
+int geometry(int64_t hq, int64_t kv, Geometry* g) {
+  if (kv <= 0 || hq <= 0 || hq % kv != 0) return SLMT_ERR_SHAPE;
+  const int64_t G = hq / kv;
+  if (G > 16) return SLMT_ERR_UNSUPPORTED;
+  int kvc = 1;
+  for (int c : {8, 4, 2}) {
+    if (kv % c == 0) {
+      kvc = c;
+      break;
+    }
+  }
+  g->G = (int)G;
+  g->nt = G <= 8 ? 1 : 2;
+  g->kvc = kvc;
+  g->ngroups = (int)(kv / kvc);
+  g->wpk = kConsumerWarps / kvc;
+  return SLMT_OK;
+}
+
+int64_t workspace_floats(int64_t slots, const Geometry& g, int D) {
+  return slots * g.wpk * (int64_t)g.kvc * g.G * (D + 2);
+}
+
+// Fill pipeline geometry, grid size and scratch pointers; launch both kernels.
+int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
+                  int64_t tiles_upper, void* workspace, int64_t workspace_bytes,
+                  void* out, int out_dtype, int64_t out_seq_stride,
+                  int64_t out_head_stride, cudaStream_t st) {
+  int dev = 0;
+  const int sms = current_device_sms(&dev);
+  if (sms <= 0) return SLMT_ERR_CUDA;
+  p.G = geo.G;
+  p.kvc = geo.kvc;
+  p.ngroups = geo.ngroups;
+  p.wpk = geo.wpk;
+  int stage_bytes;
+  if (layout == LAYOUT_PER_CHANNEL)
+    stage_bytes = geo.kvc * kTileTokens * D;
+  else
+    stage_bytes = kTileTokens * geo.kvc * (D + 8);
+  stage_bytes = round_up(stage_bytes, 128);
+  const int qbuf = round_up(geo.kvc * geo.G * D * 2, 128);
+  const int rbuf = layout == LAYOUT_PER_CHANNEL ? round_up(4 * geo.kvc * D * 2, 128) : 0;
+  const int stage_offset = round_up(kHeaderBytes + 2 * qbuf + 2 * rbuf, 128);
+  // Two resident CTAs per SM for one n-tile (register bound), one otherwise.
+  const int want_ctas = geo.nt == 1 ? 2 : 1;
+  const int budget = std::min(kSmemPerCtaMax, kSmemPerSm / want_ctas - kSmemReserved);
+  int stages = (budget - stage_offset) / stage_bytes;
+  stages = std::min(stages, 6);
+  if (stages < 2) {
+    stages = (kSmemPerCtaMax - stage_offset) / stage_bytes;
+    stages = std::min(stages, 6);
+    if (stages < 2) return SLMT_ERR_UNSUPPORTED;
+  }
+  const int smem = stage_offset + stages * stage_bytes;
+  p.stages = stages;
+  p.stage_bytes = stage_bytes;
+  p.qbuf_bytes = qbuf;
+  p.rbuf_bytes = rbuf;
+  p.stage_offset = stage_offset;
+
+  DecodeFn fn = decode_fn(D, geo.nt, layout);
+  const int occ = occupancy(dev, reinterpret_cast<const void*>(fn), smem);
+  if (occ <= 0) return SLMT_ERR_CUDA;
+  const int64_t per_sm = std::min(occ, kMaxCtasPerSm);
+  int64_t nc = (int64_t)sms * per_sm;
+  const int64_t by_work = std::max<int64_t>(1, (tiles_upper + kMinTilesPerCta - 1) / kMinTilesPerCta);
+  nc = std::max<int64_t>(1, std::min(nc, by_work));
+  p.num_ctas = (int)nc;
+
+  const int64_t slots = nc + (int64_t)geo.ngroups * p.num_seqs - 1;
+  const int64_t need = workspace_floats(slots, geo, D) * 4 + 256;
+  if (!workspace) return SLMT_ERR_WORKSPACE;
+  if (workspace_bytes < need) return SLMT_ERR_WORKSPACE;
+  uintptr_t w = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
+  p.part_acc = reinterpret_cast<float*>(w);
+  p.part_ml = p.part_acc + slots * geo.wpk * (int64_t)geo.kvc * geo.G * D;
+
+  fn<<<(unsigned)nc, kThreads, smem, st>>>(p);
+  int rc = launch_status();
+  if (rc != SLMT_OK) return rc;
+  const int64_t segs = (int64_t)geo.ngroups * p.num_seqs;
+  combine_fn(D)<<<(unsigned)segs, 256, 0, st>>>(p, out, out_dtype, out_seq_stride, out_head_stride);
+  return launch_status();
+}
+
+int check_q(const void* q, int q_dtype, int64_t seq_stride, int64_t head_stride,
+            DecodeParams& p) {
+  if (!q) return SLMT_ERR_NULL;
+  if (q_dtype != SLMT_DTYPE_F16 && q_dtype != SLMT_DTYPE_BF16) return SLMT_ERR_DTYPE;
+  if (reinterpret_cast<uintptr_t>(q) % 2 != 0) return SLMT_ERR_ALIGN;
+  p.q = q;
+  p.q_seq_stride = seq_stride;
+  p.q_head_stride = head_stride;
+  p.q_bf16 = q_dtype == SLMT_DTYPE_BF16;
+  p.q_vec16 = (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (seq_stride % 8 == 0) &&
+              (head_stride % 8 == 0);
+  return SLMT_OK;
+}
+
+int check_out(const void* out, int out_dtype) {
+  if (!out) return SLMT_ERR_NULL;
+  if (out_dtype != SLMT_DTYPE_F32 && out_dtype != SLMT_DTYPE_F16 && out_dtype != SLMT_DTYPE_BF16)
+    return SLMT_ERR_DTYPE;
+  return SLMT_OK;
+}
+
+int out_dtype_code(int out_dtype) {
+  return out_dtype == SLMT_DTYPE_F32 ? 2 : (out_dtype == SLMT_DTYPE_BF16 ? 1 : 0);
+}
+
+int contig_decode(int layout, const void* q, int q_dtype, int64_t q_seq_stride,
+                  int64_t q_head_stride, const uint8_t* k_packed,
+                  const uint8_t* v_packed, int64_t kv_seq_stride_rows,
+                  int64_t s_cap, const uint16_t* r0, const uint16_t* r1,
+                  const uint16_t* r2, const uint16_t* r3,
+                  int64_t ruler_seq_stride, int use_quant,
+                  const int32_t* seq_lens, int64_t seq_len_scalar,
+                  int causal_rows, int64_t num_seqs, int64_t hq, int64_t kv,
+                  int64_t D, float sm_scale, void* out, int out_dtype,
+                  int64_t out_seq_stride, int64_t out_head_stride,
+                  void* workspace, int64_t workspace_bytes, int32_t* err_flag,
+                  void* stream) {
+  if (!valid_head_dim(D)) return SLMT_ERR_HEAD_DIM;
+  if (num_seqs < 0 || s_cap < 0 || kv_seq_stride_rows < 0 || ruler_seq_stride < 0)
+    return SLMT_ERR_SHAPE;
+  Geometry geo;
+  int rc = geometry(hq, kv, &geo);
+  if (rc != SLMT_OK) return rc;
+  if (num_seqs == 0) return SLMT_OK;
+  if (num_seqs > INT32_MAX / 2 || s_cap > INT32_MAX / 2) return SLMT_ERR_SHAPE;
+  DecodeParams p{};
+  rc = check_q(q, q_dtype, q_seq_stride, q_head_stride, p);
+  if (rc != SLMT_OK) return rc;
+  rc = check_out(out, out_dtype);
+  if (rc != SLMT_OK) return rc;
+  if (!k_packed || !v_packed) return SLMT_ERR_NULL;
+  if (layout == LAYOUT_PER_TOKEN || use_quant) {
+    if (!r0 || !r1 || !r2 || !r3) return SLMT_ERR_NULL;
+  }
+  if (!seq_lens && seq_len_scalar < 0) return SLMT_ERR_SHAPE;
+  if (!seq_lens && seq_len_scalar > s_cap) return SLMT_ERR_SHAPE;
+  const uintptr_t ka = reinterpret_cast<uintptr_t>(k_packed), va = reinterpret_cast<uintptr_t>(v_packed);
+  if (ka % 8 != 0 || va % 8 != 0) return SLMT_ERR_ALIGN;
+  const int64_t half = D / 2;
+  p.k_codes = k_packed;
+  p.v_codes = v_packed;
+  p.kv_seq_stride_rows = kv_seq_stride_rows;
+  p.s_cap = s_cap;
+  p.r0 = r0;
+  p.r1 = r1;
+  p.r2 = r2;
+  p.r3 = r3;
+  p.ruler_seq_stride = ruler_seq_stride;
+  p.use_quant = use_quant ? 1 : 0;
+  p.contig_bulk_ok = (ka % 16 == 0) && (va % 16 == 0) && ((s_cap * half) % 16 == 0) &&
+                     ((kv_seq_stride_rows * half) % 16 == 0);
+  p.seq_lens = seq_lens;
+  p.seq_len_scalar = (int)seq_len_scalar;
+  p.causal_rows = causal_rows ? 1 : 0;
+  p.len_cap = (int)s_cap;
+  p.num_seqs = (int)num_seqs;
+  p.hq = (int)hq;
+  p.kv_total = (int)kv;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.err = err_flag;
+  const int64_t max_len = seq_lens ? s_cap : std::min<int64_t>(seq_len_scalar, s_cap);
+  const int64_t tiles_upper = num_seqs * ((max_len + 15) / 16) * geo.ngroups;
+  return launch_decode(p, layout, (int)D, geo, tiles_upper, workspace, workspace_bytes, out,
+                       out_dtype_code(out_dtype), out_seq_stride, out_head_stride,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+}  // namespace slmt
+
+using namespace slmt;
+
+extern "C" int slmt_version(void) { return 100; }
+
+extern "C" const char* slmt_status_string(int status) {
+  switch (status) {
+    case SLMT_OK:
+      return "ok";
+    case SLMT_ERR_NULL:
+      return "a required pointer is NULL";
+    case SLMT_ERR_HEAD_DIM:
+      return "head_dim must be 64/80/128";
+    case SLMT_ERR_SHAPE:
+      return "inconsistent sizes";
+    case SLMT_ERR_DTYPE:
+      return "dtype not accepted";
+    case SLMT_ERR_ALIGN:
+      return "pointer or stride alignment not met";
+    case SLMT_ERR_WORKSPACE:
+      return "workspace missing or too small";
+    case SLMT_ERR_UNSUPPORTED:
+      return "configuration not supported";
+    case SLMT_ERR_CUDA:
+      return "CUDA runtime error";
+    case SLMT_ERR_BLOCK:
+      return "BLOCK_N / BLOCK_M rejected";
+    default:
+      return "unknown status";
+  }
+}
+
+extern "C" int slmt_device_sm_count(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return SLMT_ERR_CUDA;
+  return n;
+}
+
+extern "C" int64_t slmt_decode_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
+                                               int64_t num_kv_heads, int64_t head_dim,
+                                               int device) {
+  if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
+  if (num_seqs < 0) return SLMT_ERR_SHAPE;
+  Geometry geo;
+  const int rc = geometry(num_q_heads, num_kv_heads, &geo);
+  if (rc != SLMT_OK) return rc;
+  const int sms = slmt_device_sm_count(device);
+  if (sms <= 0) return SLMT_ERR_CUDA;
+  const int64_t slots = (int64_t)sms * kMaxCtasPerSm + (int64_t)geo.ngroups * num_seqs;
+  return workspace_floats(slots, geo, (int)head_dim) * 4 + 256;
+}
+
+extern "C" int slmt_paged_decode(
+    const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+    const uint8_t* kv_cache, int64_t num_blocks, int64_t block_size,
+    int64_t num_kv_heads, int64_t head_dim, const void* block_tables,
+    int bt_dtype, int64_t bt_seq_stride, int64_t max_blocks_per_seq,
+    const int32_t* seq_lens, int64_t seq_len_scalar, int64_t max_seq_len_hint,
+    int64_t num_seqs, int64_t num_q_heads, float sm_scale, void* out,
+    int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
+    void* workspace, int64_t workspace_bytes, int32_t* err_flag, void* stream) {
+  if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
+  if (num_seqs < 0 || num_blocks < 0 || block_size <= 0 || max_blocks_per_seq < 0)
+    return SLMT_ERR_SHAPE;
+  Geometry geo;
+  int rc = geometry(num_q_heads, num_kv_heads, &geo);
+  if (rc != SLMT_OK) return rc;
+  if (num_seqs == 0) return SLMT_OK;
+  if (num_seqs > INT32_MAX / 2) return SLMT_ERR_SHAPE;
+  DecodeParams p{};
+  rc = check_q(q, q_dtype, q_seq_stride, q_head_stride, p);
+  if (rc != SLMT_OK) return rc;
+  rc = check_out(out, out_dtype);
+  if (rc != SLMT_OK) return rc;
+  if (!kv_cache || !block_tables) return SLMT_ERR_NULL;
+  if (bt_dtype != SLMT_DTYPE_I32 && bt_dtype != SLMT_DTYPE_I64) return SLMT_ERR_DTYPE;
+  if (num_seqs > 1 && bt_seq_stride < max_blocks_per_seq) return SLMT_ERR_SHAPE;
+  const int64_t cap = max_blocks_per_seq * block_size;
+  if (cap > INT32_MAX / 2) return SLMT_ERR_SHAPE;
+  if (!seq_lens && (seq_len_scalar < 0 || seq_len_scalar > cap)) return SLMT_ERR_SHAPE;
+  const uintptr_t ca = reinterpret_cast<uintptr_t>(kv_cache);
+  if (ca % 8 != 0) return SLMT_ERR_ALIGN;
+  const int64_t slot = head_dim + 8;
+  p.cache = kv_cache;
+  p.num_blocks = num_blocks;
+  p.block_size = (int)block_size;
+  p.kv_total = (int)num_kv_heads;
+  p.block_tables = block_tables;
+  p.bt_i64 = bt_dtype == SLMT_DTYPE_I64;
+  p.bt_seq_stride = bt_seq_stride;
+  p.max_blocks = (int)max_blocks_per_seq;
+  if (geo.kvc == num_kv_heads && block_size % 16 == 0 && ca % 16 == 0)
+    p.paged_mode = 0;
+  else if ((geo.kvc * slot) % 16 == 0 && (num_kv_heads * slot) % 16 == 0 && ca % 16 == 0)
+    p.paged_mode = 1;
+  else
+    p.paged_mode = 2;
+  p.seq_lens = seq_lens;
+  p.seq_len_scalar = (int)seq_len_scalar;
+  p.causal_rows = 0;
+  p.len_cap = (int)cap;
+  p.num_seqs = (int)num_seqs;
+  p.hq = (int)num_q_heads;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.err = err_flag;
+  int64_t max_len = seq_lens ? cap : seq_len_scalar;
+  if (seq_lens && max_seq_len_hint > 0) max_len = std::min(max_len, max_seq_len_hint);
+  const int64_t tiles_upper = num_seqs * ((max_len + 15) / 16) * geo.ngroups;
+  return launch_decode(p, LAYOUT_PAGED, (int)head_dim, geo, tiles_upper, workspace,
+                       workspace_bytes, out, out_dtype_code(out_dtype), out_seq_stride,
+                       out_head_stride, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int slmt_per_channel_decode(
+    const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+    const uint8_t* k_packed, const uint8_t* v_packed, int64_t kv_seq_stride_rows,
+    int64_t s_cap, const uint16_t* k_scale, const uint16_t* k_zero,
+    const uint16_t* v_scale, const uint16_t* v_zero, int64_t ruler_seq_stride,
+    int use_quant, const int32_t* seq_lens, int64_t seq_len_scalar,
+    int causal_rows, int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,
+    int64_t head_dim, float sm_scale, void* out, int out_dtype,
+    int64_t out_seq_stride, int64_t out_head_stride, void* workspace,
+    int64_t workspace_bytes, int32_t* err_flag, void* stream) {
+  return contig_decode(LAYOUT_PER_CHANNEL, q, q_dtype, q_seq_stride, q_head_stride, k_packed,
+                       v_packed, kv_seq_stride_rows, s_cap, k_scale, k_zero, v_scale, v_zero,
+                       ruler_seq_stride, use_quant, seq_lens, seq_len_scalar, causal_rows,
+                       num_seqs, num_q_heads, num_kv_heads, head_dim, sm_scale, out, out_dtype,
+                       out_seq_stride, out_head_stride, workspace, workspace_bytes, err_flag,
+                       stream);
+}
+
+extern "C" int slmt_per_token_decode(
+    const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+    const uint8_t* k_packed, const uint8_t* v_packed, int64_t kv_seq_stride_rows,
+    int64_t s_cap, const uint16_t* k_min, const uint16_t* k_step,
+    const uint16_t* v_min, const uint16_t* v_step, const int32_t* seq_lens,
+    int64_t seq_len_scalar, int64_t num_seqs, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, float sm_scale, void* out,
+    int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
+    void* workspace, int64_t workspace_bytes, int32_t* err_flag, void* stream) {
+  // rulers share the codes' row indexing: [seq, kv, s_cap]
+  return contig_decode(LAYOUT_PER_TOKEN, q, q_dtype, q_seq_stride, q_head_stride, k_packed,
+                       v_packed, kv_seq_stride_rows, s_cap, k_min, k_step, v_min, v_step,
+                       kv_seq_stride_rows, 1, seq_lens, seq_len_scalar, 0, num_seqs, num_q_heads,
+                       num_kv_heads, head_dim, sm_scale, out, out_dtype, out_seq_stride,
+                       out_head_stride, workspace, workspace_bytes, err_flag, stream);
+}
+
+extern "C" int slmt_per_channel_prefill(
+    const void* q, int q_dtype, int64_t q_head_stride, int64_t q_row_stride,
+    const uint8_t* k_packed, const uint8_t* v_packed, int64_t seq_len,
+    const uint16_t* k_scale, const uint16_t* k_zero, const uint16_t* v_scale,
+    const uint16_t* v_zero, int use_quant, int causal, int64_t num_rows,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, float sm_scale,
+    void* out, int out_dtype, int64_t out_head_stride, int64_t out_row_stride,
+    void* workspace, int64_t workspace_bytes, int32_t* err_flag, void* stream) {
+  // Query row m is a pseudo-sequence of length (causal ? min(S, m+1) : S)
+  // over the one shared K/V (sequence stride 0).
+  if (seq_len < 0 || num_rows < 0) return SLMT_ERR_SHAPE;
+  return contig_decode(LAYOUT_PER_CHANNEL, q, q_dtype, q_row_stride, q_head_stride, k_packed,
+                       v_packed, 0, seq_len, k_scale, k_zero, v_scale, v_zero, 0, use_quant,
+                       nullptr, seq_len, causal ? 1 : 0, num_rows, num_q_heads, num_kv_heads,
+                       head_dim, sm_scale, out, out_dtype, out_row_stride, out_head_stride,
+                       workspace, workspace_bytes, err_flag, stream);
+}

@@ -1,0 +1,95 @@
+// decode_common.cuh -- shared definitions of the split-K decode kernel, its
+// combine step and the host launchers.
+#pragma once
+
+#include <stdint.h>
+
+namespace slmt {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
+constexpr int kMaxStages = 8;
+constexpr int kTileTokens = 16;  // one m16 tile of tokens == one bs=16 page
+constexpr uint64_t kWaitLimitNs = 4000000000ull;      // 4 s per wait
+constexpr uint64_t kDrainLimitNs = 200000000ull;      // 0.2 s per drain wait
+
+enum Layout : int {
+  LAYOUT_PAGED = 0,        // [num_blocks, block_size, KV, D+8] per-token slots
+  LAYOUT_PER_CHANNEL = 1,  // [B, KV, S, D/2] codes + [B, KV, D] scale/zero
+  LAYOUT_PER_TOKEN = 2,    // [B, KV, S, D/2] codes + [B, KV, S] min/step
+};
+
+// One descriptor per pipeline stage, written by the producer warp.
+struct TileDesc {
+  int seq;       // sequence index, -1 = no more work
+  int kg;        // kv-head group
+  int tile;      // 16-token tile index inside the sequence
+  int nvalid;    // valid tokens in this tile (1..16)
+  int flags;     // bit0 first tile of segment, bit1 last, bit2 q buffer
+  int slot;      // partial slot (cta + segment)
+  int seg_tile;  // tile index inside this CTA's part of the segment
+  int pad;
+};
+
+struct SmemHeader {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t qfull[2];
+  uint64_t qempty[2];
+  TileDesc desc[kMaxStages];
+};
+
+constexpr int kHeaderBytes = (int)((sizeof(SmemHeader) + 127) / 128 * 128);
+
+struct DecodeParams {
+  // queries: element (seq, head, d) at q + seq*q_seq_stride + head*q_head_stride + d
+  const void* q;
+  int64_t q_seq_stride, q_head_stride;
+  int q_bf16, q_vec16;
+  // paged cache
+  const uint8_t* cache;
+  int64_t num_blocks;
+  int block_size, kv_total;
+  const void* block_tables;
+  int bt_i64;
+  int64_t bt_seq_stride;
+  int max_blocks;
+  int paged_mode;  // 0: one bulk copy per tile, 1: bulk copy per row, 2: cp.async rows
+  // contiguous layouts
+  const uint8_t* k_codes;
+  const uint8_t* v_codes;
+  int64_t kv_seq_stride_rows, s_cap;
+  const uint16_t* r0;  // per-channel k_scale | per-token k_min
+  const uint16_t* r1;  // per-channel k_zero  | per-token k_step
+  const uint16_t* r2;  // per-channel v_scale | per-token v_min
+  const uint16_t* r3;  // per-channel v_zero  | per-token v_step
+  int64_t ruler_seq_stride;
+  int use_quant, contig_bulk_ok;
+  // lengths
+  const int32_t* seq_lens;
+  int seq_len_scalar, causal_rows, len_cap;
+  // shape
+  int num_seqs, hq, G, kvc, ngroups, wpk;
+  float scale_log2;
+  // pipeline geometry
+  int stages, stage_bytes, qbuf_bytes, rbuf_bytes, stage_offset, num_ctas;
+  // split-K scratch
+  float* part_ml;   // [slots*wpk][kvc*G][2] (running max in log2 units, sum)
+  float* part_acc;  // [slots*wpk][kvc*G][D]  (unnormalised output)
+  int32_t* err;
+};
+
+__host__ __device__ inline int ntiles_of(int len) {
+  return (len + kTileTokens - 1) / kTileTokens;
+}
+
+// Largest c with floor(c*T/NC) <= t: the persistent CTA that owns tile t.
+__host__ __device__ inline int64_t cta_of_tile(int64_t t, int64_t T, int64_t NC) {
+  return ((t + 1) * NC + T - 1) / T - 1;
+}
+
+__host__ __device__ inline int64_t cta_start(int64_t c, int64_t T, int64_t NC) {
+  return c * T / NC;
+}
+
+}  // namespace slmt

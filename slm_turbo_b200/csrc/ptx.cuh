@@ -1,0 +1,182 @@
+// ptx.cuh -- thin inline-PTX wrappers used by the sm_100a kernels:
+// mbarrier pipelines, bulk (TMA 1-D) and cp.async copies into shared memory,
+// the m16n8k16 f16 tensor-core tile, movmatrix, and the 4-bit -> fp16 code
+// conversion.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace slmt {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier --
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          smem_addr(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on phase `parity`: false once `limit_ns` of wall time passed.
+// Every spin in these kernels goes through here, so no wait is endless.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// ------------------------------------------------------------ async copies --
+// 1-D bulk copy global -> shared (TMA unit), completes `bytes` of tx on `bar`.
+// src and dst 16-byte aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src,
+                                         uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// L2 policy for data streamed once (the packed cache).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
+               : "=l"(p));
+  return p;
+}
+
+// 8-byte cp.async global -> shared (both 8-byte aligned).
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)),
+               "l"(src)
+               : "memory");
+}
+
+// Arrive on `bar` once all earlier cp.async of this thread landed; the
+// barrier's expected count already includes this arrival (.noinc).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+
+// ------------------------------------------------------------ tensor cores --
+// D = A(16x16 f16, row) * B(16x8 f16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0,
+                                          uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transpose of an 8x8 b16 matrix held one row-pair per thread.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;"
+               : "=r"(y)
+               : "r"(x));
+  return y;
+}
+
+// ------------------------------------------------------ 4-bit -> fp16 codes --
+// IEEE fp16 1024 is 0x6400 and has ulp 1 on [1024, 2048), so OR-ing a nibble
+// into the low mantissa bits gives 1024+c exactly; OR-ing a nibble that sits
+// in bits 4..7 gives 1024+16c.  One LOP3 builds two such halves, one f16x2
+// subtract (or fma by 1/16, -64) makes the integers 0..15 exact.  (The
+// magic-number int4 -> fp16 conversion from the mixed-input GEMM literature,
+// e.g. Kim et al. 2022, "Who Says Elephants Can't Run".)
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask,
+                                               uint32_t orv) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(orv));
+  return d;
+}
+
+// halves = (low nibble of byte 0, low nibble of byte 2) as exact fp16
+__device__ __forceinline__ uint32_t codes_lo(uint32_t w) {
+  uint32_t t = lop_and_or(w, 0x000F000Fu, 0x64006400u), d;
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(d) : "r"(t), "r"(0x64006400u));
+  return d;
+}
+
+// halves = (high nibble of byte 0, high nibble of byte 2) as exact fp16
+__device__ __forceinline__ uint32_t codes_hi(uint32_t w) {
+  uint32_t t = lop_and_or(w, 0x00F000F0u, 0x64006400u), d;
+  // (1024 + 16c) * (1/16) + (-64) = c, one rounding, exact.
+  asm("fma.rn.f16x2 %0, %1, %2, %3;"
+      : "=r"(d)
+      : "r"(t), "r"(0x2C002C00u), "r"(0xD400D400u));
+  return d;
+}
+
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t b) {
+  return __half2float(__ushort_as_half(b));
+}
+
+}  // namespace slmt

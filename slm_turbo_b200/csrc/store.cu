@@ -1,0 +1,283 @@
+// store.cu -- quantize-on-write kernels (sm_100a).
+//
+//  * kv_store_kernel: vLLM paged per-token layout.  One warp per (token, kv
+//    head): lanes hold 2-4 dims, warp-shuffle min/max, fp32 IEEE step and
+//    codes exactly as the reference kernel computes them
+//    (kernels/kv_dequant_kernels.cuh:838-918), then each lane stores its
+//    packed bytes and lane 0 the four fp16 rulers with one 8-byte store.
+//  * pc_rulers_kernel / pc_codes_kernel: the per-channel quantizer of
+//    kernels/benchmark/benchmark.py:26-56 on the device, with the same
+//    fp16 arithmetic (each op computed in fp32 and rounded to fp16, as torch
+//    evaluates half tensors).
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace slmt {
+
+template <int D>
+__global__ void __launch_bounds__(128) kv_store_kernel(
+    const void* __restrict__ key, const void* __restrict__ value, int in_bf16,
+    int64_t tok_stride, int num_tokens, int kv, uint8_t* __restrict__ cache,
+    int64_t num_slots, const int64_t* __restrict__ slot_mapping,
+    int32_t* err) {
+  constexpr int VEC = (D == 64) ? 2 : 4;  // dims per lane
+  constexpr int LANES = D / VEC;          // active lanes (32, 32, 20)
+  constexpr int SLOT = D + 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (wid >= (int64_t)num_tokens * kv) return;
+  const int tok = (int)(wid / kv), kvh = (int)(wid % kv);
+  const int64_t slot = slot_mapping[tok];
+  if (slot < 0) return;  // padding token (ref .cuh:902)
+  if (slot >= num_slots) {
+    if (lane == 0 && err) atomicOr(reinterpret_cast<unsigned int*>(err), 2u);
+    return;
+  }
+  const int64_t row = (int64_t)tok * tok_stride + (int64_t)kvh * D;
+  const bool act = lane < LANES;
+  float xk[VEC], xv[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    xk[i] = 0.f;
+    xv[i] = 0.f;
+  }
+  if (act) {
+    if (in_bf16) {
+      const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(key) + row + lane * VEC;
+      const __nv_bfloat16* vp = reinterpret_cast<const __nv_bfloat16*>(value) + row + lane * VEC;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        xk[i] = __bfloat162float(kp[i]);
+        xv[i] = __bfloat162float(vp[i]);
+      }
+    } else {
+      const __half* kp = reinterpret_cast<const __half*>(key) + row + lane * VEC;
+      const __half* vp = reinterpret_cast<const __half*>(value) + row + lane * VEC;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        xk[i] = __half2float(kp[i]);
+        xv[i] = __half2float(vp[i]);
+      }
+    }
+  }
+  float kmn = INFINITY, kmx = -INFINITY, vmn = INFINITY, vmx = -INFINITY;
+  if (act) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      kmn = fminf(kmn, xk[i]);
+      kmx = fmaxf(kmx, xk[i]);
+      vmn = fminf(vmn, xv[i]);
+      vmx = fmaxf(vmx, xv[i]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmn = fminf(kmn, __shfl_xor_sync(0xffffffffu, kmn, o));
+    kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+    vmn = fminf(vmn, __shfl_xor_sync(0xffffffffu, vmn, o));
+    vmx = fmaxf(vmx, __shfl_xor_sync(0xffffffffu, vmx, o));
+  }
+  float kst = __fdiv_rn(kmx - kmn, 15.0f);
+  if (!(kst > 0.0f)) kst = 1.0f;  // constant row guard (ref .cuh:854)
+  float vst = __fdiv_rn(vmx - vmn, 15.0f);
+  if (!(vst > 0.0f)) vst = 1.0f;
+
+  uint8_t* base = cache + (slot * kv + kvh) * (int64_t)SLOT;
+  if (act) {
+    uint32_t kc = 0, vc = 0;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      int qk = (int)__fadd_rn(__fdiv_rn(__fsub_rn(xk[i], kmn), kst), 0.5f);
+      int qv = (int)__fadd_rn(__fdiv_rn(__fsub_rn(xv[i], vmn), vst), 0.5f);
+      qk = qk < 0 ? 0 : (qk > 15 ? 15 : qk);
+      qv = qv < 0 ? 0 : (qv > 15 ? 15 : qv);
+      kc |= (uint32_t)qk << (4 * i);
+      vc |= (uint32_t)qv << (4 * i);
+    }
+    if (VEC == 4) {
+      reinterpret_cast<uint16_t*>(base)[lane] = (uint16_t)kc;
+      reinterpret_cast<uint16_t*>(base + D / 2)[lane] = (uint16_t)vc;
+    } else {
+      base[lane] = (uint8_t)kc;
+      base[D / 2 + lane] = (uint8_t)vc;
+    }
+  }
+  if (lane == 0) {
+    const uint32_t w0 = (uint32_t)__half_as_ushort(__float2half_rn(kmn)) |
+                        ((uint32_t)__half_as_ushort(__float2half_rn(kst)) << 16);
+    const uint32_t w1 = (uint32_t)__half_as_ushort(__float2half_rn(vmn)) |
+                        ((uint32_t)__half_as_ushort(__float2half_rn(vst)) << 16);
+    *reinterpret_cast<uint2*>(base + D) = make_uint2(w0, w1);
+  }
+}
+
+// fp16 tensor arithmetic as torch evaluates it: fp32 op, round to fp16.
+__device__ __forceinline__ float h16(float x) { return __half2float(__float2half_rn(x)); }
+
+// Per (seq*kv, dim): min/max over S, then scale/zero (benchmark.py:26-42).
+__global__ void __launch_bounds__(256) pc_rulers_kernel(
+    const __half* __restrict__ x, int64_t S, int D, uint16_t* __restrict__ scale,
+    uint16_t* __restrict__ zero) {
+  __shared__ float smn[8][32], smx[8][32];
+  const int dl = threadIdx.x & 31, sg = threadIdx.x >> 5;
+  const int d = blockIdx.y * 32 + dl;
+  const int64_t row0 = (int64_t)blockIdx.x * S;
+  float mn = INFINITY, mx = -INFINITY;
+  if (d < D) {
+    for (int64_t s = sg; s < S; s += 8) {
+      const float v = __half2float(x[(row0 + s) * D + d]);
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
+  }
+  smn[sg][dl] = mn;
+  smx[sg][dl] = mx;
+  __syncthreads();
+  if (sg == 0 && d < D) {
+#pragma unroll
+    for (int k = 1; k < 8; ++k) {
+      mn = fminf(mn, smn[k][dl]);
+      mx = fmaxf(mx, smx[k][dl]);
+    }
+    float sc = h16(__fdiv_rn(h16(__fsub_rn(mx, mn)), 15.0f));
+    float zp = h16(__fsub_rn(0.0f, rintf(h16(__fdiv_rn(mn, sc)))));
+    if (mx == mn) {
+      sc = 1.0f;
+      zp = 0.0f;
+    }
+    zp = fminf(fmaxf(zp, 0.0f), 15.0f);
+    const int64_t o = (int64_t)blockIdx.x * D + d;
+    scale[o] = __half_as_ushort(__float2half_rn(sc));
+    zero[o] = __half_as_ushort(__float2half_rn(zp));
+  }
+}
+
+__device__ __forceinline__ uint32_t pc_code(float x, float sc, float zp) {
+  // q = clamp(round(x / scale) + zero, 0, 15) in fp16 steps (benchmark.py:50-52)
+  float q = h16(__fadd_rn(rintf(h16(__fdiv_rn(x, sc))), zp));
+  if (q != q) return 0u;  // NaN (scale underflow) -> 0, as the host cast gives
+  q = fminf(fmaxf(q, 0.0f), 15.0f);
+  return (uint32_t)q;
+}
+
+// codes of rows [row, row+1) for every byte: grid-stride over rows*D/2 bytes.
+// x element (h, t, d) at x + h*xh + t*xt + d; packed byte (h, pos+t, j) at
+// packed + (h*s_cap + pos + t)*D/2 + j; rulers (h, d) at scale/zero + h*D + d.
+__global__ void __launch_bounds__(256) pc_codes_kernel(
+    const __half* __restrict__ x, int64_t xh, int64_t xt, int64_t heads,
+    int64_t ntok, int D, const uint16_t* __restrict__ scale,
+    const uint16_t* __restrict__ zero, int64_t ruler_h, uint8_t* __restrict__ packed,
+    int64_t s_cap, int64_t pos) {
+  const int half = D / 2;
+  const int64_t total = heads * ntok * half;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % half);
+    const int64_t t = (i / half) % ntok;
+    const int64_t h = i / ((int64_t)half * ntok);
+    const __half* xr = x + h * xh + t * xt;
+    const int64_t ro = h * ruler_h;
+    const uint32_t c0 = pc_code(__half2float(xr[2 * j]), half_bits_to_float(scale[ro + 2 * j]),
+                                half_bits_to_float(zero[ro + 2 * j]));
+    const uint32_t c1 = pc_code(__half2float(xr[2 * j + 1]), half_bits_to_float(scale[ro + 2 * j + 1]),
+                                half_bits_to_float(zero[ro + 2 * j + 1]));
+    packed[(h * s_cap + pos + t) * half + j] = (uint8_t)(c0 | (c1 << 4));
+  }
+}
+
+}  // namespace slmt
+
+using namespace slmt;
+
+extern "C" int slmt_kv_quantize_store(const void* key, const void* value,
+                                      int kv_dtype, int64_t kv_token_stride,
+                                      int64_t num_tokens, int64_t num_kv_heads,
+                                      int64_t head_dim, uint8_t* kv_cache,
+                                      int64_t num_blocks, int64_t block_size,
+                                      const int64_t* slot_mapping,
+                                      int32_t* err_flag, void* stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks < 0)
+    return SLMT_ERR_SHAPE;
+  if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
+  if (kv_dtype != SLMT_DTYPE_F16 && kv_dtype != SLMT_DTYPE_BF16) return SLMT_ERR_DTYPE;
+  if (num_tokens == 0) return SLMT_OK;
+  if (!key || !value || !kv_cache || !slot_mapping) return SLMT_ERR_NULL;
+  if (kv_token_stride < num_kv_heads * head_dim) return SLMT_ERR_SHAPE;
+  if (reinterpret_cast<uintptr_t>(kv_cache) % 8 != 0) return SLMT_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(key) % 8 != 0 || reinterpret_cast<uintptr_t>(value) % 8 != 0 ||
+      kv_token_stride % 4 != 0)
+    return SLMT_ERR_ALIGN;
+  const int64_t warps = num_tokens * num_kv_heads;
+  if (warps > (int64_t)INT32_MAX) return SLMT_ERR_SHAPE;
+  const dim3 grid((unsigned)((warps + 3) / 4));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t num_slots = num_blocks * block_size;
+  const int bf = kv_dtype == SLMT_DTYPE_BF16;
+  switch (head_dim) {
+    case 64:
+      kv_store_kernel<64><<<grid, 128, 0, st>>>(key, value, bf, kv_token_stride, (int)num_tokens,
+                                                (int)num_kv_heads, kv_cache, num_slots, slot_mapping,
+                                                err_flag);
+      break;
+    case 80:
+      kv_store_kernel<80><<<grid, 128, 0, st>>>(key, value, bf, kv_token_stride, (int)num_tokens,
+                                                (int)num_kv_heads, kv_cache, num_slots, slot_mapping,
+                                                err_flag);
+      break;
+    default:
+      kv_store_kernel<128><<<grid, 128, 0, st>>>(key, value, bf, kv_token_stride, (int)num_tokens,
+                                                 (int)num_kv_heads, kv_cache, num_slots,
+                                                 slot_mapping, err_flag);
+      break;
+  }
+  return launch_status();
+}
+
+extern "C" int slmt_per_channel_quantize(const void* x, int x_dtype,
+                                         int64_t num_seqs, int64_t num_kv_heads,
+                                         int64_t seq_len, int64_t head_dim,
+                                         uint8_t* packed, uint16_t* scale,
+                                         uint16_t* zero, void* stream) {
+  if (num_seqs < 0 || num_kv_heads <= 0 || seq_len < 0) return SLMT_ERR_SHAPE;
+  if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
+  if (x_dtype != SLMT_DTYPE_F16) return SLMT_ERR_DTYPE;
+  if (num_seqs == 0 || seq_len == 0) return SLMT_OK;
+  if (!x || !packed || !scale || !zero) return SLMT_ERR_NULL;
+  const int64_t rows = num_seqs * num_kv_heads;
+  if (rows > 65535LL * 32768LL) return SLMT_ERR_SHAPE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 g1((unsigned)rows, (unsigned)((head_dim + 31) / 32));
+  pc_rulers_kernel<<<g1, 256, 0, st>>>(reinterpret_cast<const __half*>(x), seq_len,
+                                       (int)head_dim, scale, zero);
+  int rc = launch_status();
+  if (rc != SLMT_OK) return rc;
+  const int64_t total = rows * seq_len * (head_dim / 2);
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148LL * 16);
+  pc_codes_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+      reinterpret_cast<const __half*>(x), seq_len * head_dim, head_dim, rows, seq_len,
+      (int)head_dim, scale, zero, head_dim, packed, seq_len, 0);
+  return launch_status();
+}
+
+extern "C" int slmt_per_channel_append(const void* x, int x_dtype,
+                                       int64_t x_head_stride,
+                                       int64_t x_token_stride, int64_t num_new,
+                                       int64_t num_kv_heads, int64_t head_dim,
+                                       const uint16_t* scale,
+                                       const uint16_t* zero, uint8_t* packed,
+                                       int64_t s_cap, int64_t pos,
+                                       void* stream) {
+  if (num_new < 0 || num_kv_heads <= 0 || s_cap < 0 || pos < 0) return SLMT_ERR_SHAPE;
+  if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
+  if (x_dtype != SLMT_DTYPE_F16) return SLMT_ERR_DTYPE;
+  if (pos + num_new > s_cap) return SLMT_ERR_SHAPE;
+  if (num_new == 0) return SLMT_OK;
+  if (!x || !packed || !scale || !zero) return SLMT_ERR_NULL;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t total = num_kv_heads * num_new * (head_dim / 2);
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148LL * 16);
+  pc_codes_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+      reinterpret_cast<const __half*>(x), x_head_stride, x_token_stride, num_kv_heads, num_new,
+      (int)head_dim, scale, zero, head_dim, packed, s_cap, pos);
+  return launch_status();
+}

@@ -1,0 +1,144 @@
+"""GPU parity: per-channel quantizer, per-channel decode/prefill and contiguous
+per-token decode against the reference's golden vectors and the CPU oracle."""
+import hashlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.helpers import assert_close, f16_bits
+
+pytestmark = pytest.mark.gpu
+
+GOLD = Path(__file__).resolve().parent / "golden" / "per_channel_golden.npz"
+
+
+def _kd():
+    from slm_turbo_b200.kernels import kv_dequant
+    return kv_dequant
+
+
+def _case(z, name):
+    seed, h, kv, s, d, m = (int(x) for x in z[f"{name}/meta"])
+    torch.manual_seed(seed)
+    q = torch.randn(h, m if m else 1, d).half()
+    k = torch.randn(kv, s, d).half()
+    v = torch.randn(kv, s, d).half()
+    for key, t in (("q", q), ("k", k), ("v", v)):
+        assert hashlib.sha256(t.view(torch.int16).numpy().tobytes()).digest() == \
+            z[f"{name}/{key}_sha256"].tobytes(), f"{name}: regenerated {key} differs from the golden inputs"
+    return q, k, v, (h, kv, s, d, m)
+
+
+DECODE_CASES = ["c1_h32_kv4_s512_d64", "h14_kv2_s100_d64", "h8_kv2_s77_d80", "h16_kv8_s33_d128"]
+
+
+@pytest.mark.parametrize("name", DECODE_CASES)
+def test_device_quantizer_bit_exact(name):
+    kd = _kd()
+    z = np.load(GOLD)
+    q, k, v, _ = _case(z, name)
+    dev = torch.device("cuda")
+    for x, pk, sk, zk in ((k, "kp", "ks", "kz"), (v, "vp", "vs", "vz")):
+        packed, scale, zero = kd.kv_quantize_per_channel(x.to(dev))
+        assert (packed.cpu().numpy() == z[f"{name}/{pk}"]).all()
+        assert (f16_bits(scale) == z[f"{name}/{sk}"].view(np.uint16)).all()
+        assert (f16_bits(zero) == z[f"{name}/{zk}"].view(np.uint16)).all()
+
+
+def test_device_quantizer_special_and_append():
+    kd = _kd()
+    z = np.load(GOLD)
+    dev = torch.device("cuda")
+    x = torch.from_numpy(z["special/x"]).view(torch.float16)
+    packed, scale, zero = kd.kv_quantize_per_channel(x.to(dev))
+    assert (f16_bits(scale) == z["special/scale"].view(np.uint16)).all()
+    assert (f16_bits(zero) == z["special/zero"].view(np.uint16)).all()
+    assert (packed.cpu().numpy() == z["special/packed"]).all()
+    x_new = torch.from_numpy(z["special/x_new"]).view(torch.float16)
+    buf = torch.zeros(2, 48, 32, dtype=torch.uint8, device=dev)
+    buf[:, :40] = packed
+    kd.kv_append_per_channel(x_new.to(dev), scale, zero, buf, 40)
+    got = buf.cpu().numpy()
+    assert (got[:, 40:45] == z["special/packed_new"]).all()
+    assert (got[:, 45:] == 0).all() and (got[:, :40] == z["special/packed"]).all()
+
+
+@pytest.mark.parametrize("name", DECODE_CASES)
+@pytest.mark.parametrize("use_quant", [True, False])
+def test_per_channel_decode_vs_golden_and_oracle(name, use_quant):
+    kd = _kd()
+    z = np.load(GOLD)
+    q, k, v, (h, kv, s, d, m) = _case(z, name)
+    dev = torch.device("cuda")
+    kp = torch.from_numpy(z[f"{name}/kp"]).to(dev)
+    vp = torch.from_numpy(z[f"{name}/vp"]).to(dev)
+    rl = [torch.from_numpy(z[f"{name}/{r}"]).view(torch.float16).to(dev) for r in ("ks", "kz", "vs", "vz")]
+    out = kd.kv_dequant_decode_attention(q.to(dev), kp, *rl[:2], vp, *rl[2:], use_quant=use_quant,
+                                         num_kv_heads=kv)
+    assert out.shape == (h, 1, d) and out.dtype == torch.float32
+    got = out[:, 0].cpu().numpy()
+    want = oracle.pc_decode(q.view(1, h, d), kp.cpu()[None], rl[0].cpu()[None], rl[1].cpu()[None],
+                            vp.cpu()[None], rl[2].cpu()[None], rl[3].cpu()[None], use_quant=use_quant)[0]
+    assert_close(got, want, what=f"{name} vs oracle")
+    if use_quant:
+        # the reference's own answer: dequant(.half()) + SDPA (benchmark.py:111-117)
+        assert_close(got, z[f"{name}/out"][:, 0], what=f"{name} vs reference golden")
+
+
+def test_per_channel_decode_batched_c2_shape():
+    """BASELINE config 2 shape family: B sequences, per-sequence rulers, D=128 and 64."""
+    kd = _kd()
+    dev = torch.device("cuda")
+    for d in (128, 64):
+        g = torch.Generator().manual_seed(d)
+        B, H, KV, S = 4, 32, 8, 2048
+        q = torch.randn(B, H, d, generator=g).half()
+        k = torch.randn(B, KV, S, d, generator=g).half()
+        v = torch.randn(B, KV, S, d, generator=g).half()
+        kp, ks, kz = kd.kv_quantize_per_channel(k.to(dev))
+        vp, vs, vz = kd.kv_quantize_per_channel(v.to(dev))
+        lens = torch.tensor([2048, 1, 1000, 17], dtype=torch.int32)
+        out = kd.kv_dequant_decode_attention_batched(q.to(dev), kp, ks, kz, vp, vs, vz, seq_lens=lens.to(dev))
+        want = oracle.pc_decode(q, kp.cpu(), ks.cpu(), kz.cpu(), vp.cpu(), vs.cpu(), vz.cpu(), seq_lens=lens)
+        assert_close(out.cpu().numpy(), want, what=f"c2 d={d}")
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_vs_golden_and_oracle(causal):
+    kd = _kd()
+    z = np.load(GOLD)
+    name = "prefill_h8_kv2_s48_d64"
+    q, k, v, (h, kv, s, d, m) = _case(z, name)
+    dev = torch.device("cuda")
+    kp = torch.from_numpy(z[f"{name}/kp"]).to(dev)
+    vp = torch.from_numpy(z[f"{name}/vp"]).to(dev)
+    rl = [torch.from_numpy(z[f"{name}/{r}"]).view(torch.float16).to(dev) for r in ("ks", "kz", "vs", "vz")]
+    out = kd.kv_dequant_prefill_attention(q.to(dev), kp, *rl[:2], vp, *rl[2:], causal=causal, num_kv_heads=kv)
+    assert out.shape == (h, m, d)
+    want = oracle.pc_prefill(q, kp.cpu(), *[r.cpu() for r in rl[:2]], vp.cpu(), *[r.cpu() for r in rl[2:]],
+                             causal=causal)
+    assert_close(out.cpu().numpy(), want, what="prefill vs oracle")
+    if causal:
+        assert_close(out.cpu().numpy(), z[f"{name}/out"], what="prefill vs reference golden")
+
+
+def test_per_token_contiguous_decode():
+    kd = _kd()
+    dev = torch.device("cuda")
+    for d, h, kv, s in ((128, 32, 8, 300), (80, 8, 2, 45), (64, 16, 4, 7)):
+        g = torch.Generator().manual_seed(s)
+        q = torch.randn(h, 1, d, generator=g).half()
+        kp = torch.randint(0, 256, (kv, s, d // 2), generator=g, dtype=torch.uint8)
+        vp = torch.randint(0, 256, (kv, s, d // 2), generator=g, dtype=torch.uint8)
+        kmin = (torch.randn(kv, s, generator=g) * 2).half()
+        kstep = (torch.rand(kv, s, generator=g) * 0.5).half()
+        vmin = (torch.randn(kv, s, generator=g) * 2).half()
+        vstep = (torch.rand(kv, s, generator=g) * 0.5).half()
+        out = kd.kv_dequant_decode_per_token_attention(q.to(dev), kp.to(dev), kmin.to(dev), kstep.to(dev),
+                                                       vp.to(dev), vmin.to(dev), vstep.to(dev))
+        want = oracle.pt_decode(q.view(1, h, d), kp[None], kmin[None], kstep[None], vp[None], vmin[None],
+                                vstep[None])[0]
+        assert_close(out[:, 0].cpu().numpy(), want, what=f"per-token d={d}")
