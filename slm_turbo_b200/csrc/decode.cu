@@ -9,7 +9,7 @@ namespace slmt {
 namespace {
 
 constexpr int kMaxCtasPerSm = 4;       // cap used by the workspace bound
-constexpr int kMinTilesPerCta = 4;     // do not split below ~64 tokens per CTA
+constexpr int kMinChunksPerCta = 2;    // do not split below ~64 tokens per CTA
 constexpr int kSmemPerSm = 233472;     // 228 KB shared memory per SM (sm_100)
 constexpr int kSmemPerCtaMax = 232448; // 227 KB opt-in per CTA
 constexpr int kSmemReserved = 1024;    // reserved per resident CTA
@@ -122,7 +122,7 @@ int64_t workspace_floats(int64_t slots, const Geometry& g, int D) {
 
 // Fill pipeline geometry, grid size and scratch pointers; launch both kernels.
 int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
-                  int64_t tiles_upper, void* workspace, int64_t workspace_bytes,
+                  int64_t chunks_upper, void* workspace, int64_t workspace_bytes,
                   void* out, int out_dtype, int64_t out_seq_stride,
                   int64_t out_head_stride, cudaStream_t st) {
   int dev = 0;
@@ -134,13 +134,16 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.wpk = geo.wpk;
   int stage_bytes;
   if (layout == LAYOUT_PER_CHANNEL)
-    stage_bytes = geo.kvc * kTileTokens * D;
+    stage_bytes = geo.kvc * kChunkTokens * D;
   else
-    stage_bytes = kTileTokens * geo.kvc * (D + 8);
+    stage_bytes = kChunkTokens * geo.kvc * (D + 8);
   stage_bytes = round_up(stage_bytes, 128);
+  // q is read into registers at a segment start, so one buffer suffices; the
+  // per-channel rulers are needed again at the segment end: double buffer.
+  const int nqbuf = layout == LAYOUT_PER_CHANNEL ? 2 : 1;
   const int qbuf = round_up(geo.kvc * geo.G * D * 2, 128);
   const int rbuf = layout == LAYOUT_PER_CHANNEL ? round_up(4 * geo.kvc * D * 2, 128) : 0;
-  const int stage_offset = round_up(kHeaderBytes + 2 * qbuf + 2 * rbuf, 128);
+  const int stage_offset = round_up(kHeaderBytes + nqbuf * (qbuf + rbuf), 128);
   // Two resident CTAs per SM for one n-tile (register bound), one otherwise.
   const int want_ctas = geo.nt == 1 ? 2 : 1;
   const int budget = std::min(kSmemPerCtaMax, kSmemPerSm / want_ctas - kSmemReserved);
@@ -156,6 +159,7 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.stage_bytes = stage_bytes;
   p.qbuf_bytes = qbuf;
   p.rbuf_bytes = rbuf;
+  p.nqbuf = nqbuf;
   p.stage_offset = stage_offset;
 
   DecodeFn fn = decode_fn(D, geo.nt, layout);
@@ -163,7 +167,7 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   if (occ <= 0) return SLMT_ERR_CUDA;
   const int64_t per_sm = std::min(occ, kMaxCtasPerSm);
   int64_t nc = (int64_t)sms * per_sm;
-  const int64_t by_work = std::max<int64_t>(1, (tiles_upper + kMinTilesPerCta - 1) / kMinTilesPerCta);
+  const int64_t by_work = std::max<int64_t>(1, (chunks_upper + kMinChunksPerCta - 1) / kMinChunksPerCta);
   nc = std::max<int64_t>(1, std::min(nc, by_work));
   p.num_ctas = (int)nc;
 
@@ -178,8 +182,9 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   fn<<<(unsigned)nc, kThreads, smem, st>>>(p);
   int rc = launch_status();
   if (rc != SLMT_OK) return rc;
-  const int64_t segs = (int64_t)geo.ngroups * p.num_seqs;
-  combine_fn(D)<<<(unsigned)segs, 256, 0, st>>>(p, out, out_dtype, out_seq_stride, out_head_stride);
+  const int64_t warps = (int64_t)geo.ngroups * p.num_seqs * geo.kvc * geo.G;  // one per (segment, head)
+  combine_fn(D)<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(p, out, out_dtype, out_seq_stride,
+                                                              out_head_stride);
   return launch_status();
 }
 
@@ -264,8 +269,8 @@ int contig_decode(int layout, const void* q, int q_dtype, int64_t q_seq_stride,
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.err = err_flag;
   const int64_t max_len = seq_lens ? s_cap : std::min<int64_t>(seq_len_scalar, s_cap);
-  const int64_t tiles_upper = num_seqs * ((max_len + 15) / 16) * geo.ngroups;
-  return launch_decode(p, layout, (int)D, geo, tiles_upper, workspace, workspace_bytes, out,
+  const int64_t chunks_upper = num_seqs * ((max_len + kChunkTokens - 1) / kChunkTokens) * geo.ngroups;
+  return launch_decode(p, layout, (int)D, geo, chunks_upper, workspace, workspace_bytes, out,
                        out_dtype_code(out_dtype), out_seq_stride, out_head_stride,
                        reinterpret_cast<cudaStream_t>(stream));
 }
@@ -380,8 +385,8 @@ extern "C" int slmt_paged_decode(
   p.err = err_flag;
   int64_t max_len = seq_lens ? cap : seq_len_scalar;
   if (seq_lens && max_seq_len_hint > 0) max_len = std::min(max_len, max_seq_len_hint);
-  const int64_t tiles_upper = num_seqs * ((max_len + 15) / 16) * geo.ngroups;
-  return launch_decode(p, LAYOUT_PAGED, (int)head_dim, geo, tiles_upper, workspace,
+  const int64_t chunks_upper = num_seqs * ((max_len + kChunkTokens - 1) / kChunkTokens) * geo.ngroups;
+  return launch_decode(p, LAYOUT_PAGED, (int)head_dim, geo, chunks_upper, workspace,
                        workspace_bytes, out, out_dtype_code(out_dtype), out_seq_stride,
                        out_head_stride, reinterpret_cast<cudaStream_t>(stream));
 }

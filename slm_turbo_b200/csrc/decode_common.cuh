@@ -9,9 +9,11 @@ namespace slmt {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
 constexpr int kMaxStages = 8;
-constexpr int kTileTokens = 16;  // one m16 tile of tokens == one bs=16 page
-constexpr uint64_t kWaitLimitNs = 4000000000ull;      // 4 s per wait
-constexpr uint64_t kDrainLimitNs = 200000000ull;      // 0.2 s per drain wait
+constexpr int kTileTokens = 16;   // one m16 tensor-core tile of tokens
+constexpr int kChunkTokens = 32;  // one pipeline stage = two tiles
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
+constexpr uint64_t kDrainLimitNs = 200000000ull;  // 0.2 s per drain wait
+constexpr float kRescaleSlack = 4.0f;  // lazy softmax rescale threshold (log2 units)
 
 enum Layout : int {
   LAYOUT_PAGED = 0,        // [num_blocks, block_size, KV, D+8] per-token slots
@@ -20,14 +22,14 @@ enum Layout : int {
 };
 
 // One descriptor per pipeline stage, written by the producer warp.
-struct TileDesc {
-  int seq;       // sequence index, -1 = no more work
-  int kg;        // kv-head group
-  int tile;      // 16-token tile index inside the sequence
-  int nvalid;    // valid tokens in this tile (1..16)
-  int flags;     // bit0 first tile of segment, bit1 last, bit2 q buffer
-  int slot;      // partial slot (cta + segment)
-  int seg_tile;  // tile index inside this CTA's part of the segment
+struct ChunkDesc {
+  int seq;        // sequence index, -1 = no more work
+  int kg;         // kv-head group
+  int chunk;      // 32-token chunk index inside the sequence
+  int nvalid;     // valid tokens in this chunk (1..32)
+  int flags;      // bit0 first chunk of segment, bit1 last, bits2.. q buffer
+  int slot;       // partial slot (cta + segment)
+  int seg_chunk;  // chunk index inside this CTA's part of the segment
   int pad;
 };
 
@@ -36,7 +38,7 @@ struct SmemHeader {
   uint64_t empty[kMaxStages];
   uint64_t qfull[2];
   uint64_t qempty[2];
-  TileDesc desc[kMaxStages];
+  ChunkDesc desc[kMaxStages];
 };
 
 constexpr int kHeaderBytes = (int)((sizeof(SmemHeader) + 127) / 128 * 128);
@@ -54,7 +56,7 @@ struct DecodeParams {
   int bt_i64;
   int64_t bt_seq_stride;
   int max_blocks;
-  int paged_mode;  // 0: one bulk copy per tile, 1: bulk copy per row, 2: cp.async rows
+  int paged_mode;  // 0: one bulk copy per 16-token tile, 1: bulk copy per row, 2: cp.async rows
   // contiguous layouts
   const uint8_t* k_codes;
   const uint8_t* v_codes;
@@ -72,19 +74,19 @@ struct DecodeParams {
   int num_seqs, hq, G, kvc, ngroups, wpk;
   float scale_log2;
   // pipeline geometry
-  int stages, stage_bytes, qbuf_bytes, rbuf_bytes, stage_offset, num_ctas;
+  int stages, stage_bytes, qbuf_bytes, rbuf_bytes, nqbuf, stage_offset, num_ctas;
   // split-K scratch
   float* part_ml;   // [slots*wpk][kvc*G][2] (running max in log2 units, sum)
   float* part_acc;  // [slots*wpk][kvc*G][D]  (unnormalised output)
   int32_t* err;
 };
 
-__host__ __device__ inline int ntiles_of(int len) {
-  return (len + kTileTokens - 1) / kTileTokens;
+__host__ __device__ inline int nchunks_of(int len) {
+  return (len + kChunkTokens - 1) / kChunkTokens;
 }
 
-// Largest c with floor(c*T/NC) <= t: the persistent CTA that owns tile t.
-__host__ __device__ inline int64_t cta_of_tile(int64_t t, int64_t T, int64_t NC) {
+// Largest c with floor(c*T/NC) <= t: the persistent CTA that owns chunk t.
+__host__ __device__ inline int64_t cta_of_unit(int64_t t, int64_t T, int64_t NC) {
   return ((t + 1) * NC + T - 1) / T - 1;
 }
 
