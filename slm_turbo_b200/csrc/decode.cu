@@ -19,22 +19,34 @@ inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
 using DecodeFn = void (*)(const DecodeParams);
 using CombineFn = void (*)(const DecodeParams, void*, int, int64_t, int64_t);
 
+// The paged layout is instantiated per kv heads per stage row (KVC), so the
+// consumers' row addresses are compile-time offsets; the contiguous layouts
+// address rows with a per-warp base and need no such specialisation.
 template <int D, int NT>
-DecodeFn decode_fn_layout(int layout) {
+DecodeFn decode_fn_layout(int layout, int kvc) {
   switch (layout) {
     case LAYOUT_PAGED:
-      return decode_splitk_kernel<D, NT, LAYOUT_PAGED>;
+      switch (kvc) {
+        case 8:
+          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 8>;
+        case 4:
+          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 4>;
+        case 2:
+          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 2>;
+        default:
+          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 1>;
+      }
     case LAYOUT_PER_CHANNEL:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL>;
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL, 0>;
     default:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN>;
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN, 0>;
   }
 }
 
-DecodeFn decode_fn(int D, int nt, int layout) {
-  if (D == 64) return nt == 1 ? decode_fn_layout<64, 1>(layout) : decode_fn_layout<64, 2>(layout);
-  if (D == 80) return nt == 1 ? decode_fn_layout<80, 1>(layout) : decode_fn_layout<80, 2>(layout);
-  return nt == 1 ? decode_fn_layout<128, 1>(layout) : decode_fn_layout<128, 2>(layout);
+DecodeFn decode_fn(int D, int nt, int layout, int kvc) {
+  if (D == 64) return nt == 1 ? decode_fn_layout<64, 1>(layout, kvc) : decode_fn_layout<64, 2>(layout, kvc);
+  if (D == 80) return nt == 1 ? decode_fn_layout<80, 1>(layout, kvc) : decode_fn_layout<80, 2>(layout, kvc);
+  return nt == 1 ? decode_fn_layout<128, 1>(layout, kvc) : decode_fn_layout<128, 2>(layout, kvc);
 }
 
 CombineFn combine_fn(int D) {
@@ -162,7 +174,7 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.nqbuf = nqbuf;
   p.stage_offset = stage_offset;
 
-  DecodeFn fn = decode_fn(D, geo.nt, layout);
+  DecodeFn fn = decode_fn(D, geo.nt, layout, geo.kvc);
   const int occ = occupancy(dev, reinterpret_cast<const void*>(fn), smem);
   if (occ <= 0) return SLMT_ERR_CUDA;
   const int64_t per_sm = std::min(occ, kMaxCtasPerSm);

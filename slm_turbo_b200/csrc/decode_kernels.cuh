@@ -127,21 +127,25 @@ __device__ __forceinline__ int qk_dim(int s, int slot, int r) {
 }
 
 // Shared-memory addresses of token row t (0..31) of kv head j in a stage.
-template <int D, int LAYOUT>
+// `base` already holds the warp's kv-head offset, so with a compile-time
+// KVC every row address is base + immediate.
+template <int D, int LAYOUT, int KVC>
 struct StageView {
-  const uint8_t* st;
-  int kvc, j;
+  const uint8_t* base;  // paged: st + j*(D+8); contiguous: st + j*32*D
+  const uint8_t* rul;   // contiguous per-token rulers: st + kvc*32*D + j*8
+  int kvc;              // runtime kv heads per stage row (used when KVC == 0)
+  __device__ __forceinline__ int rs() const { return (KVC > 0 ? KVC : kvc) * (D + 8); }
   __device__ __forceinline__ const uint8_t* k(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return st + (t * kvc + j) * (D + 8);
-    return st + j * kChunkTokens * D + t * (D / 2);
+    if (LAYOUT == LAYOUT_PAGED) return base + t * rs();
+    return base + t * (D / 2);
   }
   __device__ __forceinline__ const uint8_t* v(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return st + (t * kvc + j) * (D + 8) + D / 2;
-    return st + j * kChunkTokens * D + (kChunkTokens / 2) * D + t * (D / 2);
+    if (LAYOUT == LAYOUT_PAGED) return base + t * rs() + D / 2;
+    return base + (kChunkTokens / 2) * D + t * (D / 2);
   }
   __device__ __forceinline__ const uint8_t* rulers(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return st + (t * kvc + j) * (D + 8) + D;
-    return st + kvc * kChunkTokens * D + (t * kvc + j) * 8;
+    if (LAYOUT == LAYOUT_PAGED) return base + t * rs() + D;
+    return rul + t * (KVC > 0 ? KVC : kvc) * 8;
   }
 };
 
@@ -453,16 +457,16 @@ __device__ __forceinline__ uint32_t kcodes_hi(uint32_t w) { return lop_and_or(w,
 template <int D, int NT>
 struct WarpState {
   static constexpr int KS = D / 16;
-  uint32_t qf[KS][NT][2];  // q B-fragments
+  uint4 qf[NT][(D / 8 + 3) / 4];  // q B-fragments: k-steps 2u (x, y) and 2u+1 (z, w)
   float qs[NT][2];         // log2e*scale * (sum q (per-token) | sum q'*zero (per-channel))
   float qb[NT][2];         // QK accumulator bias: sum_d q_d * (1024 | 64)
   float acc[KS][NT][4];
   float m[NT][2], l[NT][2], vs[NT][2];
 };
 
-template <int D, int NT, int LAYOUT, bool MASK>
+template <int D, int NT, int LAYOUT, int KVC, bool MASK>
 __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D, NT>& w,
-                                              const StageView<D, LAYOUT>& sv, int nvalid,
+                                              const StageView<D, LAYOUT, KVC>& sv, int nvalid,
                                               uint64_t* empty_bar) {
   constexpr int KS = D / 16;  // QK k-steps == PV m-tiles
   constexpr int QB = D / 8;   // K bytes per thread per row
@@ -479,6 +483,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
 #pragma unroll
   for (int a = 0; a < 2; ++a) {
     float c[NT][4], c2[NT][4];
+    asm volatile("" ::: "memory");  // keep the two tiles' loads from being hoisted together
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       c[nt][0] = c[nt][2] = -w.qb[nt][0];
@@ -491,27 +496,27 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     load_bytes<QB, QALIGN>(sv.k(16 * a + g + 8) + r * QB, kb);
 #pragma unroll
     for (int u = 0; u < QW; ++u) {
+      uint4 qf[NT];  // B-fragments of k-steps 2u (x, y) and 2u+1 (z, w)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) qf[nt] = w.qf[nt][u];
       if (4 * u + 4 <= QB) {
         uint32_t a0 = kcodes_lo(ka[u]), a1 = kcodes_lo(kb[u]);
         uint32_t a2 = kcodes_hi(ka[u]), a3 = kcodes_hi(kb[u]);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-          mma_16816(c[nt], a0, a1, a2, a3, w.qf[2 * u][nt][0], w.qf[2 * u][nt][1]);
+        for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
         const uint32_t sa = ka[u] >> 8, sb = kb[u] >> 8;
         a0 = kcodes_lo(sa);
         a1 = kcodes_lo(sb);
         a2 = kcodes_hi(sa);
         a3 = kcodes_hi(sb);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-          mma_16816(c2[nt], a0, a1, a2, a3, w.qf[2 * u + 1][nt][0], w.qf[2 * u + 1][nt][1]);
+        for (int nt = 0; nt < NT; ++nt) mma_16816(c2[nt], a0, a1, a2, a3, qf[nt].z, qf[nt].w);
       } else {
         const uint32_t sa = __byte_perm(ka[u], 0u, 0x3120), sb = __byte_perm(kb[u], 0u, 0x3120);
         const uint32_t a0 = kcodes_lo(sa), a1 = kcodes_lo(sb);
         const uint32_t a2 = kcodes_hi(sa), a3 = kcodes_hi(sb);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-          mma_16816(c[nt], a0, a1, a2, a3, w.qf[2 * u][nt][0], w.qf[2 * u][nt][1]);
+        for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
       }
     }
 #pragma unroll
@@ -520,21 +525,21 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
       for (int i = 0; i < 4; ++i) sacc[a][nt][i] = c[nt][i] + c2[nt][i];
   }
 
-  // ---- rulers of tokens 16a+g (+8h), packed: x = (k_min, k_step), y = (v_min, v_step) ----
-  uint2 rw[2][2];
+  // ---- per-token rulers (k_min, k_step | v_min, v_step) are read from shared
+  // memory where they are used, to keep registers free ----
+  auto ruler_k = [&](int a, int h) -> float2 {
+    if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(p.use_quant ? -1.f : 0.f, 1.f);
+    return __half22float2(*reinterpret_cast<const __half2*>(sv.rulers(16 * a + g + 8 * h)));
+  };
+  auto ruler_v = [&](int a, int h) -> float2 {
+    if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(0.f, 1.f);
+    return __half22float2(*reinterpret_cast<const __half2*>(sv.rulers(16 * a + g + 8 * h) + 4));
+  };
   bool val[2][2];
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
+  for (int a = 0; a < 2; ++a)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int t = 16 * a + g + 8 * h;
-      val[a][h] = !MASK || t < nvalid;
-      if (LAYOUT == LAYOUT_PER_CHANNEL)
-        rw[a][h] = make_uint2(p.use_quant ? 0x3C00BC00u : 0x3C000000u, 0x3C000000u);  // (-1|0, 1), (0, 1)
-      else
-        rw[a][h] = *reinterpret_cast<const uint2*>(sv.rulers(t));
-    }
-  }
+    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * a + g + 8 * h) < nvalid;
 
   // ---- scores + online softmax (log2 domain, lazy rescale) ----
   const float sl2 = p.scale_log2;
@@ -546,7 +551,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   for (int a = 0; a < 2; ++a) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float2 kr = __half22float2(*reinterpret_cast<const __half2*>(&rw[a][h].x));
+      const float2 kr = ruler_k(a, h);
       const float kst = kr.y * sl2;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -600,7 +605,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int h = i >> 1, e = i & 1;
-        const float2 vr = __half22float2(*reinterpret_cast<const __half2*>(&rw[a][h].y));
+        const float2 vr = ruler_v(a, h);
         const float pe = exp2_approx(sc[a][nt][i] - w.m[nt][e]);  // 0 for masked rows
         w.l[nt][e] += pe;
         if (MASK) {
@@ -616,28 +621,25 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     }
   }
 
-  // ---- V codes of the chunk into registers; then the stage can be reused ----
+  // ---- PV on raw codes: O^T[dims x heads] += V^T . P'^T, one k-step per tile ----
   // thread (g, r) needs tokens 16a + {2r, 2r+1, 2r+8, 2r+9}, bytes [g*VB, +VB)
-  uint32_t vw[2][4][VW];
 #pragma unroll
   for (int a = 0; a < 2; ++a) {
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r) + g * VB, vw[a][0]);
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 1) + g * VB, vw[a][1]);
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 8) + g * VB, vw[a][2]);
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 9) + g * VB, vw[a][3]);
-  }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(empty_bar);
-
-  // ---- PV on raw codes: O^T[dims x heads] += V^T . P'^T, two k-steps ----
-#pragma unroll
-  for (int a = 0; a < 2; ++a) {
+    uint32_t vw[4][VW];
+    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r) + g * VB, vw[0]);
+    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 1) + g * VB, vw[1]);
+    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 8) + g * VB, vw[2]);
+    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 9) + g * VB, vw[3]);
+    if (a == 1) {  // every shared-memory read of the stage is done: release it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar);
+    }
 #pragma unroll
     for (int u = 0; u < VW; ++u) {
-      const uint32_t x = __byte_perm(vw[a][0][u], vw[a][1][u], 0x5410);
-      const uint32_t y = __byte_perm(vw[a][0][u], vw[a][1][u], 0x7632);
-      const uint32_t x2 = __byte_perm(vw[a][2][u], vw[a][3][u], 0x5410);
-      const uint32_t y2 = __byte_perm(vw[a][2][u], vw[a][3][u], 0x7632);
+      const uint32_t x = __byte_perm(vw[0][u], vw[1][u], 0x5410);
+      const uint32_t y = __byte_perm(vw[0][u], vw[1][u], 0x7632);
+      const uint32_t x2 = __byte_perm(vw[2][u], vw[3][u], 0x5410);
+      const uint32_t y2 = __byte_perm(vw[2][u], vw[3][u], 0x7632);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int mt = 4 * u + k;
@@ -654,7 +656,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   }
 }
 
-template <int D, int NT, int LAYOUT>
+template <int D, int NT, int LAYOUT, int KVC>
 __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
                                 const uint8_t* qbuf, const uint8_t* rbuf,
                                 const uint8_t* stg) {
@@ -663,7 +665,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, r = lane & 3;
-  const int kvc = p.kvc, G = p.G;
+  const int kvc = KVC > 0 ? KVC : p.kvc, G = p.G;
   const int j = warp & (kvc - 1), wsub = warp / kvc;  // kvc and wpk are powers of two
   const int wmask = p.wpk - 1;
 
@@ -676,11 +678,13 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       if (lane == 0) set_err(p, 4u);
       return;
     }
-    const ChunkDesc d = hdr->desc[stage];
-    if (d.seq < 0) break;
-    const int qbi = d.flags >> 2;
+    const ChunkDesc& dsm = hdr->desc[stage];
+    if (dsm.seq < 0) break;
+    // fields needed after the stage is released are copied to registers
+    const int flags = dsm.flags, slot = dsm.slot, nvalid = dsm.nvalid, seg_chunk = dsm.seg_chunk;
+    const int qbi = flags >> 2;
 
-    if (d.flags & 1) {
+    if (flags & 1) {
       // ---- segment start: q fragments, q sums, fresh softmax state ----
       if (!mbar_wait(&hdr->qfull[qbi], (seg / (uint32_t)p.nqbuf) & 1u, kWaitLimitNs)) {
         if (lane == 0) set_err(p, 4u);
@@ -715,8 +719,13 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
               x[e] = v;
             }
           }
-          w.qf[s][nt][0] = pack_half2(x[0], x[1]);
-          w.qf[s][nt][1] = pack_half2(x[2], x[3]);
+          if (s & 1) {
+            w.qf[nt][s >> 1].z = pack_half2(x[0], x[1]);
+            w.qf[nt][s >> 1].w = pack_half2(x[2], x[3]);
+          } else {
+            w.qf[nt][s >> 1].x = pack_half2(x[0], x[1]);
+            w.qf[nt][s >> 1].y = pack_half2(x[2], x[3]);
+          }
         }
       }
 #pragma unroll
@@ -745,23 +754,32 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       }
     }
 
-    if ((d.seg_chunk & wmask) == wsub) {
-      StageView<D, LAYOUT> sv{stg + (size_t)stage * p.stage_bytes, kvc, j};
-      if (d.nvalid == kChunkTokens)
-        consume_chunk<D, NT, LAYOUT, false>(p, w, sv, d.nvalid, &hdr->empty[stage]);
+    if ((seg_chunk & wmask) == wsub) {
+      const uint8_t* st = stg + (size_t)stage * p.stage_bytes;
+      StageView<D, LAYOUT, KVC> sv;
+      sv.kvc = kvc;
+      if (LAYOUT == LAYOUT_PAGED) {
+        sv.base = st + j * (D + 8);
+        sv.rul = nullptr;
+      } else {
+        sv.base = st + j * kChunkTokens * D;
+        sv.rul = st + kvc * kChunkTokens * D + j * 8;
+      }
+      if (nvalid == kChunkTokens)
+        consume_chunk<D, NT, LAYOUT, KVC, false>(p, w, sv, nvalid, &hdr->empty[stage]);
       else
-        consume_chunk<D, NT, LAYOUT, true>(p, w, sv, d.nvalid, &hdr->empty[stage]);
+        consume_chunk<D, NT, LAYOUT, KVC, true>(p, w, sv, nvalid, &hdr->empty[stage]);
     } else {
       __syncwarp();
       if (lane == 0) mbar_arrive(&hdr->empty[stage]);
     }
 
-    if (d.flags & 2) {
+    if (flags & 2) {
       // ---- segment end: finish the sums and write the split-K partial ----
       const __half* vsc = reinterpret_cast<const __half*>(rbuf + qbi * p.rbuf_bytes) + (size_t)(2 * kvc + j) * D;
       const __half* vze = vsc + (size_t)kvc * D;
       const int hg = kvc * G;
-      const int64_t slotw = (int64_t)d.slot * p.wpk + wsub;
+      const int64_t slotw = (int64_t)slot * p.wpk + wsub;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         float l0 = w.l[nt][0], l1 = w.l[nt][1], u0 = w.vs[nt][0], u1 = w.vs[nt][1];
@@ -816,7 +834,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 // One n-tile: two CTAs (18 warps) per SM, which caps registers at 96 (a
 // sub-partition holds up to 5 warps of its 16K registers); two n-tiles run one
 // CTA per SM.
-template <int D, int NT, int LAYOUT>
+template <int D, int NT, int LAYOUT, int KVC>
 __global__ void __launch_bounds__(kThreads, (NT == 1) ? 2 : 1)
     decode_splitk_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -839,7 +857,7 @@ __global__ void __launch_bounds__(kThreads, (NT == 1) ? 2 : 1)
   if (threadIdx.x >= kConsumerWarps * 32)
     decode_producer<D, LAYOUT>(p, hdr, qbuf, rbuf, stg);
   else
-    decode_consumer<D, NT, LAYOUT>(p, hdr, qbuf, rbuf, stg);
+    decode_consumer<D, NT, LAYOUT, KVC>(p, hdr, qbuf, rbuf, stg);
 }
 
 // ------------------------------------------------------------------- combine --
