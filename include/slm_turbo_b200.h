@@ -72,6 +72,10 @@ int slmt_device_sm_count(int device);
 /*
  * Bytes of split-K scratch the decode entry points need for `num_seqs`
  * sequences (pseudo-sequences for prefill) on `device`; negative on error.
+ * The scratch must be zero-filled before its first use (it holds per-segment
+ * arrival counters, which every completed call leaves at zero again), must
+ * be 256-byte aligned, and must not be shared by calls that overlap on the
+ * GPU.  If a call reports a device error, zero it again before reuse.
  */
 int64_t slmt_decode_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
                                     int64_t num_kv_heads, int64_t head_dim,

@@ -110,13 +110,23 @@ def device_state(device: torch.device) -> _DeviceState:
     return st
 
 
+_ws_need: dict = {}
+
+
 def workspace(device: torch.device, num_seqs: int, hq: int, kv: int, d: int) -> torch.Tensor:
-    """Split-K scratch for a decode call (grown, never shrunk, per device)."""
+    """Split-K scratch for a decode call (grown, never shrunk, per device).
+
+    Allocated zero-filled: it holds the per-segment arrival counters, which
+    the kernel leaves at zero after every complete call."""
     st = device_state(device)
-    need = load().slmt_decode_workspace_bytes(num_seqs, hq, kv, d, st.device.index)
-    check(int(need) if need < 0 else 0, "slmt_decode_workspace_bytes")
+    key = (st.device.index, num_seqs, hq, kv, d)
+    need = _ws_need.get(key)
+    if need is None:
+        need = int(load().slmt_decode_workspace_bytes(num_seqs, hq, kv, d, st.device.index))
+        check(need if need < 0 else 0, "slmt_decode_workspace_bytes")
+        _ws_need[key] = need
     if st.workspace.numel() < need:
-        st.workspace = torch.empty(int(need), dtype=torch.uint8, device=st.device)
+        st.workspace = torch.zeros(need, dtype=torch.uint8, device=st.device)
     return st.workspace
 
 
@@ -125,9 +135,13 @@ def error_word(device: torch.device) -> torch.Tensor:
 
 
 def read_device_errors(device, reset: bool = True) -> int:
-    """Synchronise and return the kernels' error bits (SLMT_DEVERR_*)."""
-    e = error_word(torch.device(device))
-    v = int(e.item())
+    """Synchronise and return the kernels' error bits (SLMT_DEVERR_*).
+
+    After an error the scratch counters may be left non-zero by an aborted
+    launch, so the workspace is zeroed again together with the error word."""
+    st = device_state(torch.device(device))
+    v = int(st.err.item())
     if reset and v:
-        e.zero_()
+        st.err.zero_()
+        st.workspace.zero_()
     return v

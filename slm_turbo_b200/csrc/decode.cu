@@ -8,7 +8,6 @@ namespace slmt {
 
 namespace {
 
-constexpr int kMaxCtasPerSm = 4;       // cap used by the workspace bound
 constexpr int kMinChunksPerCta = 2;    // do not split below ~64 tokens per CTA
 constexpr int kSmemPerSm = 233472;     // 228 KB shared memory per SM (sm_100)
 constexpr int kSmemPerCtaMax = 232448; // 227 KB opt-in per CTA
@@ -17,29 +16,35 @@ constexpr int kSmemReserved = 1024;    // reserved per resident CTA
 inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
 using DecodeFn = void (*)(const DecodeParams);
-using CombineFn = void (*)(const DecodeParams, void*, int, int64_t, int64_t);
 
 // The paged layout is instantiated per kv heads per stage row (KVC), so the
 // consumers' row addresses are compile-time offsets; the contiguous layouts
 // address rows with a per-warp base and need no such specialisation.
-template <int D, int NT>
-DecodeFn decode_fn_layout(int layout, int kvc) {
+template <int D, int NT, int KVC>
+DecodeFn decode_fn_kvc(int layout) {
   switch (layout) {
     case LAYOUT_PAGED:
-      switch (kvc) {
-        case 8:
-          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 8>;
-        case 4:
-          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 4>;
-        case 2:
-          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 2>;
-        default:
-          return decode_splitk_kernel<D, NT, LAYOUT_PAGED, 1>;
-      }
+      return decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC>;
     case LAYOUT_PER_CHANNEL:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL, 0>;
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL, KVC>;
     default:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN, 0>;
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN, KVC>;
+  }
+}
+
+// Instantiated per head dim, n-tiles and kv heads per CTA (compile-time
+// row strides, one consumer warp per kv head).
+template <int D, int NT>
+DecodeFn decode_fn_layout(int layout, int kvc) {
+  switch (kvc) {
+    case 8:
+      return decode_fn_kvc<D, NT, 8>(layout);
+    case 4:
+      return decode_fn_kvc<D, NT, 4>(layout);
+    case 2:
+      return decode_fn_kvc<D, NT, 2>(layout);
+    default:
+      return decode_fn_kvc<D, NT, 1>(layout);
   }
 }
 
@@ -47,12 +52,6 @@ DecodeFn decode_fn(int D, int nt, int layout, int kvc) {
   if (D == 64) return nt == 1 ? decode_fn_layout<64, 1>(layout, kvc) : decode_fn_layout<64, 2>(layout, kvc);
   if (D == 80) return nt == 1 ? decode_fn_layout<80, 1>(layout, kvc) : decode_fn_layout<80, 2>(layout, kvc);
   return nt == 1 ? decode_fn_layout<128, 1>(layout, kvc) : decode_fn_layout<128, 2>(layout, kvc);
-}
-
-CombineFn combine_fn(int D) {
-  if (D == 64) return decode_combine_kernel<64>;
-  if (D == 80) return decode_combine_kernel<80>;
-  return decode_combine_kernel<128>;
 }
 
 struct OccEntry {
@@ -68,7 +67,7 @@ int g_occ_n = 0;
 
 // Resident CTAs per SM for `fn` at `smem` bytes (opts the kernel into large
 // dynamic shared memory the first time it is seen on a device).
-int occupancy(int device, const void* fn, int smem) {
+int occupancy(int device, const void* fn, int threads, int smem) {
   std::lock_guard<std::mutex> lk(g_occ_mu);
   for (int i = 0; i < g_occ_n; ++i)
     if (g_occ[i].device == device && g_occ[i].fn == fn && g_occ[i].smem == smem) return g_occ[i].occ;
@@ -76,7 +75,7 @@ int occupancy(int device, const void* fn, int smem) {
       cudaSuccess)
     return -1;
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, smem) != cudaSuccess) return -1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess) return -1;
   if (g_occ_n < 256) g_occ[g_occ_n++] = OccEntry{device, fn, smem, occ};
   return occ;
 }
@@ -106,7 +105,7 @@ int current_device_sms(int* device_out) {
 namespace {
 
 struct Geometry {
-  int G, nt, kvc, ngroups, wpk;
+  int G, nt, kvc, ngroups;
 };
 
 int geometry(int64_t hq, int64_t kv, Geometry* g) {
@@ -124,12 +123,19 @@ int geometry(int64_t hq, int64_t kv, Geometry* g) {
   g->nt = G <= 8 ? 1 : 2;
   g->kvc = kvc;
   g->ngroups = (int)(kv / kvc);
-  g->wpk = kConsumerWarps / kvc;
   return SLMT_OK;
 }
 
 int64_t workspace_floats(int64_t slots, const Geometry& g, int D) {
-  return slots * g.wpk * (int64_t)g.kvc * g.G * (D + 2);
+  return slots * (int64_t)g.kvc * g.G * (D + 2);
+}
+
+// Scratch layout: [segment arrival counters (int32, zero between calls)]
+// [partial rows (float) D per head] [partial (m, l) pairs], 256-byte aligned.
+int64_t counter_bytes(int64_t segments) { return (segments * 4 + 255) / 256 * 256; }
+
+int64_t workspace_total(int64_t slots, int64_t segments, const Geometry& g, int D) {
+  return counter_bytes(segments) + workspace_floats(slots, g, D) * 4 + 256;
 }
 
 // Fill pipeline geometry, grid size and scratch pointers; launch both kernels.
@@ -142,8 +148,10 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   if (sms <= 0) return SLMT_ERR_CUDA;
   p.G = geo.G;
   p.kvc = geo.kvc;
+  // one bulk copy per (sequence, group) when the group's heads are contiguous
+  p.q_bulk = (reinterpret_cast<uintptr_t>(p.q) % 16 == 0) && (p.q_head_stride == D) &&
+             ((p.q_seq_stride * 2) % 16 == 0);
   p.ngroups = geo.ngroups;
-  p.wpk = geo.wpk;
   int stage_bytes;
   if (layout == LAYOUT_PER_CHANNEL)
     stage_bytes = geo.kvc * kChunkTokens * D;
@@ -156,8 +164,8 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   const int qbuf = round_up(geo.kvc * geo.G * D * 2, 128);
   const int rbuf = layout == LAYOUT_PER_CHANNEL ? round_up(4 * geo.kvc * D * 2, 128) : 0;
   const int stage_offset = round_up(kHeaderBytes + nqbuf * (qbuf + rbuf), 128);
-  // Two resident CTAs per SM for one n-tile (register bound), one otherwise.
-  const int want_ctas = geo.nt == 1 ? 2 : 1;
+  const int want_ctas = ctas_per_sm(geo.kvc, geo.nt);
+  const int threads = cta_threads(geo.kvc);
   const int budget = std::min(kSmemPerCtaMax, kSmemPerSm / want_ctas - kSmemReserved);
   int stages = (budget - stage_offset) / stage_bytes;
   stages = std::min(stages, 6);
@@ -175,28 +183,30 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.stage_offset = stage_offset;
 
   DecodeFn fn = decode_fn(D, geo.nt, layout, geo.kvc);
-  const int occ = occupancy(dev, reinterpret_cast<const void*>(fn), smem);
+  const int occ = occupancy(dev, reinterpret_cast<const void*>(fn), threads, smem);
   if (occ <= 0) return SLMT_ERR_CUDA;
-  const int64_t per_sm = std::min(occ, kMaxCtasPerSm);
+  const int64_t per_sm = std::min(occ, ctas_per_sm(geo.kvc, geo.nt));  // keeps the workspace bound
   int64_t nc = (int64_t)sms * per_sm;
   const int64_t by_work = std::max<int64_t>(1, (chunks_upper + kMinChunksPerCta - 1) / kMinChunksPerCta);
   nc = std::max<int64_t>(1, std::min(nc, by_work));
   p.num_ctas = (int)nc;
 
-  const int64_t slots = nc + (int64_t)geo.ngroups * p.num_seqs - 1;
-  const int64_t need = workspace_floats(slots, geo, D) * 4 + 256;
+  const int64_t segments = (int64_t)geo.ngroups * p.num_seqs;
+  const int64_t slots = nc + segments - 1;
+  const int64_t need = workspace_total(slots, segments, geo, D);
   if (!workspace) return SLMT_ERR_WORKSPACE;
   if (workspace_bytes < need) return SLMT_ERR_WORKSPACE;
-  uintptr_t w = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
-  p.part_acc = reinterpret_cast<float*>(w);
-  p.part_ml = p.part_acc + slots * geo.wpk * (int64_t)geo.kvc * geo.G * D;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return SLMT_ERR_ALIGN;
+  uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
+  p.seg_count = reinterpret_cast<int32_t*>(w);
+  p.part_acc = reinterpret_cast<float*>(w + counter_bytes(segments));
+  p.part_ml = p.part_acc + slots * (int64_t)geo.kvc * geo.G * D;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.out_seq_stride = out_seq_stride;
+  p.out_head_stride = out_head_stride;
 
-  fn<<<(unsigned)nc, kThreads, smem, st>>>(p);
-  int rc = launch_status();
-  if (rc != SLMT_OK) return rc;
-  const int64_t warps = (int64_t)geo.ngroups * p.num_seqs * geo.kvc * geo.G;  // one per (segment, head)
-  combine_fn(D)<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(p, out, out_dtype, out_seq_stride,
-                                                              out_head_stride);
+  fn<<<(unsigned)nc, threads, smem, st>>>(p);
   return launch_status();
 }
 
@@ -209,8 +219,7 @@ int check_q(const void* q, int q_dtype, int64_t seq_stride, int64_t head_stride,
   p.q_seq_stride = seq_stride;
   p.q_head_stride = head_stride;
   p.q_bf16 = q_dtype == SLMT_DTYPE_BF16;
-  p.q_vec16 = (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (seq_stride % 8 == 0) &&
-              (head_stride % 8 == 0);
+  p.q_bulk = 0;  // decided once the head dim and group size are known
   return SLMT_OK;
 }
 
@@ -338,8 +347,9 @@ extern "C" int64_t slmt_decode_workspace_bytes(int64_t num_seqs, int64_t num_q_h
   if (rc != SLMT_OK) return rc;
   const int sms = slmt_device_sm_count(device);
   if (sms <= 0) return SLMT_ERR_CUDA;
-  const int64_t slots = (int64_t)sms * kMaxCtasPerSm + (int64_t)geo.ngroups * num_seqs;
-  return workspace_floats(slots, geo, (int)head_dim) * 4 + 256;
+  const int64_t segments = (int64_t)geo.ngroups * num_seqs;
+  const int64_t slots = (int64_t)sms * ctas_per_sm(geo.kvc, geo.nt) + segments;
+  return workspace_total(slots, segments, geo, (int)head_dim);
 }
 
 extern "C" int slmt_paged_decode(

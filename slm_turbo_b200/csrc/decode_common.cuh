@@ -1,13 +1,17 @@
-// decode_common.cuh -- shared definitions of the split-K decode kernel, its
-// combine step and the host launchers.
+// decode_common.cuh -- shared definitions of the split-K decode kernel (its
+// in-launch partial merge included) and the host launchers.
 #pragma once
 
 #include <stdint.h>
 
 namespace slmt {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
+// A CTA has one consumer warp per kv head of its group (KVC of them, 1..8)
+// and one producer warp.
+__host__ __device__ constexpr int cta_threads(int kvc) { return (kvc + 1) * 32; }
+__host__ __device__ constexpr int ctas_per_sm(int kvc, int nt) {
+  return ((nt == 1) ? 18 : 9) / (kvc + 1) > 0 ? ((nt == 1) ? 18 : 9) / (kvc + 1) : 1;
+}
 constexpr int kMaxStages = 8;
 constexpr int kTileTokens = 16;   // one m16 tensor-core tile of tokens
 constexpr int kChunkTokens = 32;  // one pipeline stage = two tiles
@@ -29,9 +33,19 @@ struct ChunkDesc {
   int nvalid;     // valid tokens in this chunk (1..32)
   int flags;      // bit0 first chunk of segment, bit1 last, bits2.. q buffer
   int slot;       // partial slot (cta + segment)
-  int seg_chunk;  // chunk index inside this CTA's part of the segment
-  int pad;
+  int ncov;       // CTAs whose chunk ranges cover this segment
+  int c_first;    // first of them
+  int pad[4];
 };
+
+// A segment whose partials this CTA merges after its main loop.
+struct MergeJob {
+  int e_seg, seq, kg, c_first, ncov;
+};
+
+// A CTA writes a partial (and may have to merge) only for a segment that
+// other CTAs also stream: at most its first and its last segment.
+constexpr int kMaxMerges = 4;
 
 struct SmemHeader {
   uint64_t full[kMaxStages];
@@ -39,6 +53,8 @@ struct SmemHeader {
   uint64_t qfull[2];
   uint64_t qempty[2];
   ChunkDesc desc[kMaxStages];
+  int nmerge;
+  MergeJob merges[kMaxMerges];
 };
 
 constexpr int kHeaderBytes = (int)((sizeof(SmemHeader) + 127) / 128 * 128);
@@ -47,7 +63,7 @@ struct DecodeParams {
   // queries: element (seq, head, d) at q + seq*q_seq_stride + head*q_head_stride + d
   const void* q;
   int64_t q_seq_stride, q_head_stride;
-  int q_bf16, q_vec16;
+  int q_bf16, q_bulk;  // q_bulk: a group's q rows are one 16-byte aligned span
   // paged cache
   const uint8_t* cache;
   int64_t num_blocks;
@@ -71,14 +87,19 @@ struct DecodeParams {
   const int32_t* seq_lens;
   int seq_len_scalar, causal_rows, len_cap;
   // shape
-  int num_seqs, hq, G, kvc, ngroups, wpk;
+  int num_seqs, hq, G, kvc, ngroups;
   float scale_log2;
   // pipeline geometry
   int stages, stage_bytes, qbuf_bytes, rbuf_bytes, nqbuf, stage_offset, num_ctas;
   // split-K scratch
-  float* part_ml;   // [slots*wpk][kvc*G][2] (running max in log2 units, sum)
-  float* part_acc;  // [slots*wpk][kvc*G][D]  (unnormalised output)
+  float* part_ml;      // [slots][kvc*G][2] (running max in log2 units, sum)
+  float* part_acc;     // [slots][kvc*G][D]  (unnormalised output)
+  int32_t* seg_count;  // [ngroups*B] arrivals per segment; zero between launches
   int32_t* err;
+  // output element (seq, head, d) at out + seq*out_seq_stride + head*out_head_stride + d
+  void* out;
+  int out_dtype;  // 0 f16, 1 bf16, 2 f32
+  int64_t out_seq_stride, out_head_stride;
 };
 
 __host__ __device__ inline int nchunks_of(int len) {

@@ -5,15 +5,14 @@
 // CTA c owns the contiguous chunk range [c*T/NC, (c+1)*T/NC), so every CTA
 // streams the same number of bytes whatever the length mix of the batch.
 //
-// Warp roles (288 threads):
-//   warp 8      producer: walks its chunk range and stages each chunk with
+// Warp roles ((KVC + 1) x 32 threads, KVC = kv heads per group):
+//   warp KVC    producer: walks its chunk range and stages each chunk with
 //               1-D bulk copies (TMA unit; one per 16-token page tile, or per
 //               row / cp.async when the layout is not 16-byte aligned) into a
 //               STAGES-deep shared-memory ring guarded by mbarriers; stages
 //               q (+ per-channel rulers) once per segment.
-//   warps 0..7  consumers: warp w owns kv head w % KVC of the group and the
-//               chunks with seg_chunk % WPK == w / KVC.  Per 32-token chunk
-//               (two m16 tiles, independent tensor-core chains):
+//   warps 0..KVC-1  consumers: warp w owns kv head w of the group.  Per
+//               32-token chunk (two m16 tiles, independent tensor-core chains):
 //                 S^T[16 tok x 8 heads] = codes(K) . q            (m16n8k16, fp32)
 //                 s = k_step*S + k_min*sum(q)                      (per-token rulers)
 //                 online softmax, log2 domain, lazy rescale (quad shuffles)
@@ -22,8 +21,12 @@
 //                 sum_v += p*v_min
 //               4-bit codes go straight from shared memory to exact fp16
 //               integers in registers; no dequantised K/V exists anywhere.
-//   At a segment end each consumer warp writes (m, l, acc) to the split-K
-//   scratch slot cta+segment; decode_combine_kernel merges the slots.
+//   At a segment end: a segment that one CTA streamed alone is normalised and
+//   written straight to the output; otherwise each consumer warp writes
+//   (m, l, acc) to the split-K scratch slot cta+segment, the CTA counts itself
+//   in the segment's arrival counter, and the last CTA to arrive merges all
+//   partials (log-sum-exp weights), writes the output rows and resets the
+//   counter -- no separate combine launch.
 #pragma once
 
 #include "decode_common.cuh"
@@ -127,29 +130,58 @@ __device__ __forceinline__ int qk_dim(int s, int slot, int r) {
 }
 
 // Shared-memory addresses of token row t (0..31) of kv head j in a stage.
-// `base` already holds the warp's kv-head offset, so with a compile-time
-// KVC every row address is base + immediate.
+// `base` already holds the warp's kv-head offset, so every row address is
+// base + immediate.
 template <int D, int LAYOUT, int KVC>
 struct StageView {
   const uint8_t* base;  // paged: st + j*(D+8); contiguous: st + j*32*D
-  const uint8_t* rul;   // contiguous per-token rulers: st + kvc*32*D + j*8
-  int kvc;              // runtime kv heads per stage row (used when KVC == 0)
-  __device__ __forceinline__ int rs() const { return (KVC > 0 ? KVC : kvc) * (D + 8); }
+  const uint8_t* rul;   // contiguous per-token rulers: st + KVC*32*D + j*8
   __device__ __forceinline__ const uint8_t* k(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return base + t * rs();
+    if (LAYOUT == LAYOUT_PAGED) return base + t * KVC * (D + 8);
     return base + t * (D / 2);
   }
   __device__ __forceinline__ const uint8_t* v(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return base + t * rs() + D / 2;
+    if (LAYOUT == LAYOUT_PAGED) return base + t * KVC * (D + 8) + D / 2;
     return base + (kChunkTokens / 2) * D + t * (D / 2);
   }
   __device__ __forceinline__ const uint8_t* rulers(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return base + t * rs() + D;
-    return rul + t * (KVC > 0 ? KVC : kvc) * 8;
+    if (LAYOUT == LAYOUT_PAGED) return base + t * KVC * (D + 8) + D;
+    return rul + t * KVC * 8;
   }
 };
 
 // ------------------------------------------------------------------ producer --
+// Page ids of 32 consecutive 16-token tiles of sequence s, one per lane.
+__device__ __forceinline__ int64_t page_window(const DecodeParams& p, int s, int tile0, int ntile) {
+  const int lane = threadIdx.x & 31;
+  const int pt = tile0 + lane;
+  return (pt < ntile) ? block_entry(p, s, (pt * kTileTokens) / p.block_size) : 0;
+}
+
+// Next non-empty segment after (s, kg): one warp-wide load of 32 lengths.
+// Returns false when none of the next 32 sequences has tokens (caller loops).
+__device__ __forceinline__ bool next_segment(const DecodeParams& p, int s, int kg, int& s2, int& kg2,
+                                             int& L2) {
+  const int lane = threadIdx.x & 31;
+  const int B = p.num_seqs;
+  const int raw = s + 1 + lane;
+  const int ls = raw % B;
+  const int Ll = seq_len_of(p, ls);
+  const unsigned m = __ballot_sync(0xffffffffu, Ll > 0);
+  if (m == 0) {
+    s2 = (s + 32) % B;
+    kg2 = kg + (s + 32) / B;
+    L2 = 0;
+    return false;
+  }
+  const int src = __ffs(m) - 1;
+  const int r2 = s + 1 + src;
+  s2 = r2 % B;
+  kg2 = kg + r2 / B;
+  L2 = __shfl_sync(0xffffffffu, Ll, src);
+  return true;
+}
+
 template <int D, int LAYOUT>
 __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
                                 uint8_t* qbuf, uint8_t* rbuf, uint8_t* stg) {
@@ -171,8 +203,22 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     t_seq += warp_sum_i(n);
   }
   const long long T = t_seq * p.ngroups;
-  const long long t_begin = cta_start(c, T, p.num_ctas);
-  const long long t_end = cta_start(c + 1, T, p.num_ctas);
+  // never more CTAs than chunks, so every working CTA owns at least one
+  const long long nc_eff = T < p.num_ctas ? T : p.num_ctas;
+  const long long t_begin = c < nc_eff ? cta_start(c, T, nc_eff) : 0;
+  const long long t_end = c < nc_eff ? cta_start(c + 1, T, nc_eff) : 0;
+
+  // sequences without tokens get zeros (no segment ever writes them)
+  for (int b = c; b < B; b += gridDim.x) {
+    if (seq_len_of(p, b) != 0) continue;
+    for (int i = lane; i < p.hq * D; i += 32) {
+      const int64_t o = (int64_t)b * p.out_seq_stride + (int64_t)(i / D) * p.out_head_stride + i % D;
+      if (p.out_dtype == 2)
+        reinterpret_cast<float*>(p.out)[o] = 0.f;
+      else
+        reinterpret_cast<uint16_t*>(p.out)[o] = 0;
+    }
+  }
 
   const uint64_t policy = l2_evict_first_policy();
   uint32_t it = 0;
@@ -183,7 +229,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
   if (t_begin < t_end) {
     int kg = (int)(t_begin / t_seq);
     const long long tt = t_begin - (long long)kg * t_seq;
-    // Locate the sequence holding chunk tt of group kg.
+    // Locate the sequence holding chunk tt of group kg (second pass hits L1).
     int s = 0;
     long long ps = 0;
     for (int base = 0; base < B; base += 32) {
@@ -204,10 +250,27 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     int L = seq_len_of(p, s);
     int nch = nchunks_of(L);
     bool first = true;
-    int seg_chunk = 0;
-    uint32_t seg = 0;   // segments started by this CTA
-    int pg_base = 0;    // first tile whose page id lane 0 of pg_cache holds
-    int64_t pg_cache = 0;
+    uint32_t seg = 0;  // segments started by this CTA
+    int seg_ncov = 1, seg_cfirst = c;
+
+    // prefetched state: page-id windows of this segment (current, next) and
+    // the next segment's length and first window
+    const bool pg_mode0 = (LAYOUT == LAYOUT_PAGED) && p.paged_mode == 0;
+    int pg_base = 2 * chunk;
+    int64_t pg_cur = 0, pg_nxt = 0, pg_seg = 0;
+    int ns = 0, nkg = 0, nL = 0;
+    bool have_next = false;
+    if (pg_mode0) {
+      const int ntile = (L + kTileTokens - 1) / kTileTokens;
+      pg_cur = page_window(p, s, pg_base, ntile);
+      pg_nxt = page_window(p, s, pg_base + 32, ntile);
+    }
+    auto prefetch_next_segment = [&]() {
+      have_next = next_segment(p, s, kg, ns, nkg, nL);
+      if (pg_mode0 && have_next && nkg < p.ngroups)
+        pg_seg = page_window(p, ns, 0, (nL + kTileTokens - 1) / kTileTokens);
+    };
+    prefetch_next_segment();
 
     for (long long t = t_begin; t < t_end; ++t) {
       if (it >= (uint32_t)p.stages) {
@@ -218,57 +281,11 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       }
       const int qb = (int)(seg % (uint32_t)p.nqbuf);
       if (first) {
-        // ---- stage q (fp16) and per-channel rulers of this segment ----
-        const uint32_t use = seg / (uint32_t)p.nqbuf;
-        if (use >= 1) {
-          if (!mbar_wait(&hdr->qempty[qb], (use - 1) & 1u, kWaitLimitNs)) {
-            failed = true;
-            break;
-          }
-        }
-        const int hg = p.kvc * p.G;  // q heads of the group
-        __half* qd = reinterpret_cast<__half*>(qbuf + qb * p.qbuf_bytes);
-        const int64_t qrow0 = (int64_t)s * p.q_seq_stride + (int64_t)kg * hg * p.q_head_stride;
-        if (p.q_vec16 && !p.q_bf16) {
-          const int per_head = D / 8;
-          for (int i = lane; i < hg * per_head; i += 32) {
-            const int h = i / per_head, c8 = i % per_head;
-            const __half* src = reinterpret_cast<const __half*>(p.q) + qrow0 +
-                                (int64_t)h * p.q_head_stride + c8 * 8;
-            reinterpret_cast<uint4*>(qd + h * D)[c8] = *reinterpret_cast<const uint4*>(src);
-          }
-        } else {
-          for (int i = lane; i < hg * D; i += 32) {
-            const int h = i / D, d = i % D;
-            const int64_t off = qrow0 + (int64_t)h * p.q_head_stride + d;
-            float v;
-            if (p.q_bf16)
-              v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[off]);
-            else
-              v = __half2float(reinterpret_cast<const __half*>(p.q)[off]);
-            qd[h * D + d] = __float2half_rn(v);
-          }
-        }
-        if (LAYOUT == LAYOUT_PER_CHANNEL) {
-          uint16_t* rd = reinterpret_cast<uint16_t*>(rbuf + qb * p.rbuf_bytes);
-          for (int i = lane; i < 4 * p.kvc * D; i += 32) {
-            const int a = i / (p.kvc * D), rem = i % (p.kvc * D);
-            const int jj = rem / D, d = rem % D;
-            const int kvh = kg * p.kvc + jj;
-            uint16_t v;
-            if (p.use_quant) {
-              const uint16_t* src = (a == 0) ? p.r0 : (a == 1) ? p.r1 : (a == 2) ? p.r2 : p.r3;
-              v = src[(int64_t)s * p.ruler_seq_stride + (int64_t)kvh * D + d];
-            } else {
-              v = (a & 1) ? (uint16_t)0 : (uint16_t)0x3C00u;  // scale 1, zero 0
-            }
-            rd[i] = v;
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&hdr->qfull[qb]);
+        // CTAs whose ranges cover this segment (its chunk 0 is global chunk t - chunk)
+        const long long p0 = t - chunk;
+        seg_cfirst = (int)cta_of_unit(p0, T, nc_eff);
+        seg_ncov = (int)cta_of_unit(p0 + nch - 1, T, nc_eff) - seg_cfirst + 1;
       }
-
       const bool last = (chunk == nch - 1) || (t == t_end - 1);
       const int nvalid = min(kChunkTokens, L - chunk * kChunkTokens);
       const int flags = (first ? 1 : 0) | (last ? 2 : 0) | (qb << 2);
@@ -280,17 +297,17 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       if (LAYOUT == LAYOUT_PAGED) {
         const int bs = p.block_size;
         const int row_bytes = p.kvc * SLOT;
-        if (p.paged_mode == 0) {
-          // tiles 2*chunk, 2*chunk+1; page ids of 32 tiles per warp load
+        if (pg_mode0) {
+          // tiles 2*chunk, 2*chunk+1: page ids from the prefetched windows
           const int t0 = 2 * chunk;
-          const int ntile = (L + kTileTokens - 1) / kTileTokens;
-          if (first || t0 + 1 - pg_base >= 32) {
-            pg_base = t0;
-            const int pt = t0 + lane;
-            pg_cache = (pt < ntile) ? block_entry(p, s, (pt * kTileTokens) / bs) : 0;
+          if (t0 - pg_base >= 32) {
+            pg_base += 32;
+            pg_cur = pg_nxt;
+            pg_nxt = page_window(p, s, pg_base + 32, (L + kTileTokens - 1) / kTileTokens);
           }
-          const int64_t ph0 = __shfl_sync(0xffffffffu, pg_cache, t0 - pg_base);
-          const int64_t ph1 = __shfl_sync(0xffffffffu, pg_cache, t0 + 1 - pg_base);
+          const int ntile = (L + kTileTokens - 1) / kTileTokens;
+          const int64_t ph0 = __shfl_sync(0xffffffffu, pg_cur, t0 - pg_base);
+          const int64_t ph1 = __shfl_sync(0xffffffffu, pg_cur, t0 + 1 - pg_base);
           const bool has1 = t0 + 1 < ntile;
           const bool ok0 = ph0 >= 0 && ph0 < p.num_blocks;
           const bool ok1 = has1 && ph1 >= 0 && ph1 < p.num_blocks;
@@ -298,21 +315,18 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           const uint32_t tile_bytes = (uint32_t)(kTileTokens * row_bytes);
           const uint32_t tx = (ok0 ? tile_bytes : 0u) + (ok1 ? tile_bytes : 0u);
           if (lane == 0) {
-            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_chunk, 0};
+            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, {0, 0, 0, 0}};
           }
           __syncwarp();
           if (lane == 0) {
             mbar_arrive_expect_tx(fb, tx);
-            if (ok0) {
-              const int tok = tok0;
-              bulk_g2s(dst, p.cache + ((ph0 * bs + tok % bs) * p.kv_total) * (int64_t)SLOT, tile_bytes, fb,
+            if (ok0)
+              bulk_g2s(dst, p.cache + ((ph0 * bs + tok0 % bs) * p.kv_total) * (int64_t)SLOT, tile_bytes, fb,
                        policy);
-            }
-            if (ok1) {
-              const int tok = tok0 + kTileTokens;
-              bulk_g2s(dst + tile_bytes, p.cache + ((ph1 * bs + tok % bs) * p.kv_total) * (int64_t)SLOT,
+            if (ok1)
+              bulk_g2s(dst + tile_bytes,
+                       p.cache + ((ph1 * bs + (tok0 + kTileTokens) % bs) * p.kv_total) * (int64_t)SLOT,
                        tile_bytes, fb, policy);
-            }
           }
         } else {
           // one row (token) per lane
@@ -328,7 +342,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           }
           const unsigned okm = __ballot_sync(0xffffffffu, ok);
           if (lane == 0) {
-            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_chunk, 0};
+            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, {0, 0, 0, 0}};
           }
           const uint8_t* src =
               p.cache + ((phys * bs + (tok % bs)) * p.kv_total + (int64_t)kg * p.kvc) * SLOT;
@@ -366,7 +380,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           }
         }
         if (lane == 0) {
-          hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_chunk, 0};
+          hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, {0, 0, 0, 0}};
         }
         const uint32_t tx = bulk ? (uint32_t)(2 * p.kvc * bytes) : 0u;
         __syncwarp();
@@ -393,28 +407,81 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       }
       cp_async_arrive_noinc(fb);
 
+      if (first) {
+        // ---- q (raw fp16/bf16) and per-channel rulers of this segment, staged
+        // after the segment's first chunk is already in flight ----
+        const uint32_t use = seg / (uint32_t)p.nqbuf;
+        if (use >= 1) {
+          if (!mbar_wait(&hdr->qempty[qb], (use - 1) & 1u, kWaitLimitNs)) {
+            failed = true;
+            ++it;
+            break;
+          }
+        }
+        const int hg = p.kvc * p.G;  // q heads of the group
+        uint8_t* qd = qbuf + qb * p.qbuf_bytes;
+        const int64_t qrow0 = (int64_t)s * p.q_seq_stride + (int64_t)kg * hg * p.q_head_stride;
+        const uint16_t* qsrc = reinterpret_cast<const uint16_t*>(p.q) + qrow0;
+        uint32_t qtx = 0;
+        if (p.q_bulk)
+          qtx = (uint32_t)(hg * D * 2);
+        else
+          for (int i = lane; i < hg * D; i += 32)
+            reinterpret_cast<uint16_t*>(qd)[i] = qsrc[(int64_t)(i / D) * p.q_head_stride + i % D];
+        if (LAYOUT == LAYOUT_PER_CHANNEL) {
+          uint16_t* rd = reinterpret_cast<uint16_t*>(rbuf + qb * p.rbuf_bytes);
+          for (int i = lane; i < 4 * p.kvc * D; i += 32) {
+            const int a = i / (p.kvc * D), rem = i % (p.kvc * D);
+            const int jj = rem / D, d = rem % D;
+            const int kvh = kg * p.kvc + jj;
+            uint16_t v;
+            if (p.use_quant) {
+              const uint16_t* src = (a == 0) ? p.r0 : (a == 1) ? p.r1 : (a == 2) ? p.r2 : p.r3;
+              v = src[(int64_t)s * p.ruler_seq_stride + (int64_t)kvh * D + d];
+            } else {
+              v = (a & 1) ? (uint16_t)0 : (uint16_t)0x3C00u;  // scale 1, zero 0
+            }
+            rd[i] = v;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&hdr->qfull[qb], qtx);
+          if (qtx) bulk_g2s(qd, qsrc, qtx, &hdr->qfull[qb], policy);
+        }
+      }
+
       ++it;
       if (++stage == p.stages) {
         stage = 0;
         phase ^= 1u;
       }
       first = false;
-      ++seg_chunk;
       ++chunk;
       if (chunk == nch && t + 1 < t_end) {
-        // next non-empty segment
-        do {
-          if (++s == B) {
-            s = 0;
-            ++kg;
+        // next non-empty segment (prefetched when this one started)
+        if (!have_next) {  // 32 empty sequences in a row: keep scanning
+          while (!have_next) {
+            s = ns;
+            kg = nkg;
+            have_next = next_segment(p, s, kg, ns, nkg, nL);
           }
-          L = seq_len_of(p, s);
-          nch = nchunks_of(L);
-        } while (nch == 0);
+          if (pg_mode0) pg_seg = page_window(p, ns, 0, (nL + kTileTokens - 1) / kTileTokens);
+        }
+        s = ns;
+        kg = nkg;
+        L = nL;
+        nch = nchunks_of(L);
         chunk = 0;
         first = true;
-        seg_chunk = 0;
         ++seg;
+        if (pg_mode0) {
+          const int ntile = (L + kTileTokens - 1) / kTileTokens;
+          pg_base = 0;
+          pg_cur = pg_seg;
+          pg_nxt = page_window(p, s, 32, ntile);
+        }
+        prefetch_next_segment();
       }
     }
   }
@@ -443,6 +510,120 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
   }
 }
 
+// Output element store in the requested dtype (0 f16, 1 bf16, 2 f32).
+__device__ __forceinline__ void store_out(const DecodeParams& p, int64_t off, float v) {
+  if (p.out_dtype == 2)
+    reinterpret_cast<float*>(p.out)[off] = v;
+  else if (p.out_dtype == 1)
+    reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(v);
+}
+
+// Barrier of the CTA's consumer threads only (the producer warp never joins).
+template <int NCW>
+__device__ __forceinline__ void consumer_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
+}
+
+// The CTA's consumer threads merge segment `job` from the partials of CTAs
+// c_first .. c_first+ncov-1 and write its output rows.  Work goes in passes
+// over groups of heads and batches of partials sized to the scratch `scr`
+// (the idle stage ring).  Per pass: one round of L2 reads (cp.async.cg for
+// the partial rows, ld.global.cg for the (m, l) pairs -- coherent with the
+// other CTAs' stores), then every thread folds the batch into the output
+// quads it owns, computing the log-sum-exp weights of their heads itself.
+template <int D, int KVC>
+__device__ void merge_segment(const DecodeParams& p, const MergeJob& job, float* scr, int scr_floats) {
+  constexpr int NTHR = KVC * 32;
+  constexpr int Q = D / 4;
+  constexpr int IPT = 4;  // output quads per thread per pass
+  const int tid = threadIdx.x;
+  const int hg = p.kvc * p.G;
+  const int np = job.ncov;
+  int nb = min(np, 16);
+  while (nb > 1 && nb * (D + 2) > scr_floats) nb >>= 1;
+  const int hp = max(1, min(min(hg, scr_floats / (nb * (D + 2))), IPT * NTHR / Q));
+  const int64_t row0 = (int64_t)(job.c_first + job.e_seg) * hg;  // partial i, head h: row0 + i*hg + h
+  const float4* acc4 = reinterpret_cast<const float4*>(p.part_acc);
+  const float2* ml2 = reinterpret_cast<const float2*>(p.part_ml);
+  float* sRow = scr;                 // [nb][hp][D]
+  float2* sMl = reinterpret_cast<float2*>(scr + nb * hp * D);  // [nb][hp]
+  for (int h0 = 0; h0 < hg; h0 += hp) {
+    const int hb = min(hp, hg - h0);
+    float4 a[IPT];
+    float M[IPT], L[IPT];
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      M[k] = -INFINITY;
+      L[k] = 0.f;
+    }
+    for (int p0 = 0; p0 < np; p0 += nb) {
+      const int nbb = min(nb, np - p0);
+      for (int i = 0; i < nbb; ++i) {
+        const int64_t r = row0 + (int64_t)(p0 + i) * hg + h0;
+        for (int t = tid; t < hb * Q; t += NTHR) cp_async16_cg(sRow + (i * hp * D + 4 * t), acc4 + r * Q + t);
+      }
+      // (m, l) pairs: two loads in flight per thread before either store, so
+      // no thread serialises on one L2 round trip per partial.
+      for (int t = tid; t < nbb * hb; t += 2 * NTHR) {
+        const int t1 = t + NTHR;
+        const int i0 = t / hb, i1 = t1 / hb;
+        const float2 v0 = __ldcg(ml2 + row0 + (int64_t)(p0 + i0) * hg + h0 + (t - i0 * hb));
+        float2 v1 = make_float2(0.f, 0.f);
+        if (t1 < nbb * hb) v1 = __ldcg(ml2 + row0 + (int64_t)(p0 + i1) * hg + h0 + (t1 - i1 * hb));
+        sMl[i0 * hp + (t - i0 * hb)] = v0;
+        if (t1 < nbb * hb) sMl[i1 * hp + (t1 - i1 * hb)] = v1;
+      }
+      cp_async_wait_all();
+      consumer_bar<KVC>();
+#pragma unroll
+      for (int k = 0; k < IPT; ++k) {
+        const int item = k * NTHR + tid;
+        if (item < hb * Q) {
+          const int h = item / Q;
+          float mx = M[k];
+          for (int i = 0; i < nbb; ++i) mx = fmaxf(mx, sMl[i * hp + h].x);
+          if (mx != -INFINITY) {
+            const float sc = (M[k] == -INFINITY) ? 0.f : exp2_approx(M[k] - mx);
+            float4 v = make_float4(a[k].x * sc, a[k].y * sc, a[k].z * sc, a[k].w * sc);
+            float l = L[k] * sc;
+            for (int i = 0; i < nbb; ++i) {
+              const float2 ml = sMl[i * hp + h];
+              const float w = (ml.x == -INFINITY) ? 0.f : exp2_approx(ml.x - mx);
+              const float4 x = *reinterpret_cast<const float4*>(sRow + (i * hp * D + 4 * item));
+              l += w * ml.y;
+              v.x += w * x.x;
+              v.y += w * x.y;
+              v.z += w * x.z;
+              v.w += w * x.w;
+            }
+            a[k] = v;
+            L[k] = l;
+            M[k] = mx;
+          }
+        }
+      }
+      consumer_bar<KVC>();
+    }
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      const int item = k * NTHR + tid;
+      if (item < hb * Q) {
+        const int h = item / Q, q = item % Q;
+        const float inv = (L[k] > 0.f) ? 1.f / L[k] : 0.f;
+        const int64_t o = (int64_t)job.seq * p.out_seq_stride +
+                          (int64_t)(job.kg * hg + h0 + h) * p.out_head_stride + 4 * q;
+        store_out(p, o, a[k].x * inv);
+        store_out(p, o + 1, a[k].y * inv);
+        store_out(p, o + 2, a[k].z * inv);
+        store_out(p, o + 3, a[k].w * inv);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ consumer --
 // K codes enter QK with the magic-number bias left in: the low nibble as
 // fp16 1024+c, the high nibble as 64+c (exponent 0x54, nibble in mantissa
@@ -467,7 +648,7 @@ struct WarpState {
 template <int D, int NT, int LAYOUT, int KVC, bool MASK>
 __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D, NT>& w,
                                               const StageView<D, LAYOUT, KVC>& sv, int nvalid,
-                                              uint64_t* empty_bar) {
+                                              uint64_t* empty_bar, bool release) {
   constexpr int KS = D / 16;  // QK k-steps == PV m-tiles
   constexpr int QB = D / 8;   // K bytes per thread per row
   constexpr int VB = D / 16;  // V bytes per thread per row
@@ -565,19 +746,22 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
       }
     }
   }
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx[nt][0] = fmaxf(mx[nt][0], __shfl_xor_sync(0xffffffffu, mx[nt][0], o));
-      mx[nt][1] = fmaxf(mx[nt][1], __shfl_xor_sync(0xffffffffu, mx[nt][1], o));
-    }
-  }
+  // Each thread checks its own scores against the running max; only when
+  // some score exceeds it by more than the slack is the head max reduced
+  // across the 8 lanes that share the head column and the state rescaled.
   bool need = false;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
     need |= (mx[nt][0] > w.m[nt][0] + kRescaleSlack) || (mx[nt][1] > w.m[nt][1] + kRescaleSlack);
   if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx[nt][0] = fmaxf(mx[nt][0], __shfl_xor_sync(0xffffffffu, mx[nt][0], o));
+        mx[nt][1] = fmaxf(mx[nt][1], __shfl_xor_sync(0xffffffffu, mx[nt][1], o));
+      }
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -630,7 +814,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 1) + g * VB, vw[1]);
     load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 8) + g * VB, vw[2]);
     load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 9) + g * VB, vw[3]);
-    if (a == 1) {  // every shared-memory read of the stage is done: release it
+    if (a == 1 && release) {  // every shared-memory read of the stage is done: release it
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar);
     }
@@ -665,9 +849,9 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, r = lane & 3;
-  const int kvc = KVC > 0 ? KVC : p.kvc, G = p.G;
-  const int j = warp & (kvc - 1), wsub = warp / kvc;  // kvc and wpk are powers of two
-  const int wmask = p.wpk - 1;
+  constexpr int kvc = KVC;
+  const int G = p.G;
+  const int j = warp;  // one consumer warp per kv head of the group
 
   WarpState<D, NT> w;
   int stage = 0;
@@ -681,7 +865,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
     const ChunkDesc& dsm = hdr->desc[stage];
     if (dsm.seq < 0) break;
     // fields needed after the stage is released are copied to registers
-    const int flags = dsm.flags, slot = dsm.slot, nvalid = dsm.nvalid, seg_chunk = dsm.seg_chunk;
+    const int flags = dsm.flags, slot = dsm.slot, nvalid = dsm.nvalid;
     const int qbi = flags >> 2;
 
     if (flags & 1) {
@@ -706,7 +890,9 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int dd = qk_dim<D>(s, e, r);
-              float v = __half2float(qh[n * D + dd]);
+              const uint16_t raw = reinterpret_cast<const uint16_t*>(qh)[n * D + dd];
+              float v = p.q_bf16 ? __half2float(__float2half_rn(__bfloat162float(__ushort_as_bfloat16(raw))))
+                                 : half_bits_to_float(raw);
               if (LAYOUT == LAYOUT_PER_CHANNEL) {
                 if (p.use_quant) {
                   v = __half2float(__float2half_rn(v * __half2float(ksc[dd])));
@@ -754,10 +940,9 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       }
     }
 
-    if ((seg_chunk & wmask) == wsub) {
+    {
       const uint8_t* st = stg + (size_t)stage * p.stage_bytes;
       StageView<D, LAYOUT, KVC> sv;
-      sv.kvc = kvc;
       if (LAYOUT == LAYOUT_PAGED) {
         sv.base = st + j * (D + 8);
         sv.rul = nullptr;
@@ -765,21 +950,26 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
         sv.base = st + j * kChunkTokens * D;
         sv.rul = st + kvc * kChunkTokens * D + j * 8;
       }
+      // a segment's last chunk keeps its stage (and descriptor) until the
+      // segment's output or partial is written
+      const bool rel = !(flags & 2);
       if (nvalid == kChunkTokens)
-        consume_chunk<D, NT, LAYOUT, KVC, false>(p, w, sv, nvalid, &hdr->empty[stage]);
+        consume_chunk<D, NT, LAYOUT, KVC, false>(p, w, sv, nvalid, &hdr->empty[stage], rel);
       else
-        consume_chunk<D, NT, LAYOUT, KVC, true>(p, w, sv, nvalid, &hdr->empty[stage]);
-    } else {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&hdr->empty[stage]);
+        consume_chunk<D, NT, LAYOUT, KVC, true>(p, w, sv, nvalid, &hdr->empty[stage], rel);
     }
 
     if (flags & 2) {
-      // ---- segment end: finish the sums and write the split-K partial ----
+      // ---- segment end: write the output, or a partial + maybe merge ----
+      const ChunkDesc& dd = hdr->desc[stage];  // still owned: released below
+      const int ncov = dd.ncov, c_first = dd.c_first;
+      const int e_seg = dd.kg * p.num_seqs + dd.seq;
+      const int seq = dd.seq, kgrp = dd.kg;
       const __half* vsc = reinterpret_cast<const __half*>(rbuf + qbi * p.rbuf_bytes) + (size_t)(2 * kvc + j) * D;
       const __half* vze = vsc + (size_t)kvc * D;
       const int hg = kvc * G;
-      const int64_t slotw = (int64_t)slot * p.wpk + wsub;
+      const bool direct = ncov == 1;
+      const int64_t slotw = slot;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         float l0 = w.l[nt][0], l1 = w.l[nt][1], u0 = w.vs[nt][0], u1 = w.vs[nt][1];
@@ -797,10 +987,13 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
           const float vsum = e ? u1 : u0;
           if (n < G) {
             const int64_t row = slotw * hg + (int64_t)j * G + n;
-            if (g == 0) {
+            if (!direct && g == 0) {
               p.part_ml[row * 2 + 0] = w.m[nt][e];
               p.part_ml[row * 2 + 1] = lsum;
             }
+            const float inv = (direct && lsum > 0.f) ? 1.f / lsum : 1.f;
+            const int64_t obase = (int64_t)seq * p.out_seq_stride +
+                                  (int64_t)(kgrp * hg + j * G + n) * p.out_head_stride + 2 * g * VB;
             float* dst = p.part_acc + row * D + 2 * g * VB;
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
@@ -811,7 +1004,30 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
                 o0 = __half2float(vsc[d0]) * (o0 - __half2float(vze[d0]) * lsum);
                 o1 = __half2float(vsc[d0 + 1]) * (o1 - __half2float(vze[d0 + 1]) * lsum);
               }
-              reinterpret_cast<float2*>(dst)[mt] = make_float2(o0, o1);
+              if (direct) {
+                store_out(p, obase + 2 * mt, o0 * inv);
+                store_out(p, obase + 2 * mt + 1, o1 * inv);
+              } else {
+                reinterpret_cast<float2*>(dst)[mt] = make_float2(o0, o1);
+              }
+            }
+          }
+        }
+      }
+      if (!direct) {
+        // publish the partial; the last CTA to finish the segment merges it
+        // after its main loop (recorded in the shared merge list)
+        __threadfence();
+        consumer_bar<KVC>();
+        if (threadIdx.x == 0) {
+          const int old = (ncov == 1) ? 0 : atomicAdd(reinterpret_cast<int*>(p.seg_count) + e_seg, 1);
+          if (old == ncov - 1) {
+            const int k = hdr->nmerge;
+            if (k < kMaxMerges) {
+              hdr->merges[k] = MergeJob{e_seg, seq, kgrp, c_first, ncov};
+              hdr->nmerge = k + 1;
+            } else {
+              set_err(p, 16u);  // cannot happen: bounded by the host (see kMaxMerges)
             }
           }
         }
@@ -820,6 +1036,8 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
         __syncwarp();
         if (lane == 0) mbar_arrive(&hdr->qempty[qbi]);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&hdr->empty[stage]);
       ++seg;
     }
 
@@ -828,14 +1046,27 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       phase ^= 1u;
     }
   }
+
+  // ---- merges of the segments this CTA finished last (the stage ring is
+  // idle now: every copy has landed and been consumed) ----
+  consumer_bar<KVC>();
+  const int nm = hdr->nmerge;
+  if (nm > 0) __threadfence();
+  for (int k = 0; k < nm; ++k) {
+    const MergeJob job = hdr->merges[k];
+    merge_segment<D, KVC>(p, job, reinterpret_cast<float*>(const_cast<uint8_t*>(stg)),
+                          p.stages * p.stage_bytes / 4);
+    if (threadIdx.x == 0 && job.ncov > 1) p.seg_count[job.e_seg] = 0;
+  }
 }
 
 // -------------------------------------------------------------------- kernel --
-// One n-tile: two CTAs (18 warps) per SM, which caps registers at 96 (a
-// sub-partition holds up to 5 warps of its 16K registers); two n-tiles run one
-// CTA per SM.
+// KVC consumer warps (one per kv head of the group) + 1 producer warp.  The
+// CTAs per SM are chosen for about 18 warps per SM with one n-tile (96
+// registers: a sub-partition holds up to 5 warps of its 16K registers) and
+// about 9 with two n-tiles.
 template <int D, int NT, int LAYOUT, int KVC>
-__global__ void __launch_bounds__(kThreads, (NT == 1) ? 2 : 1)
+__global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
     decode_splitk_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   SmemHeader* hdr = reinterpret_cast<SmemHeader*>(smem);
@@ -845,129 +1076,20 @@ __global__ void __launch_bounds__(kThreads, (NT == 1) ? 2 : 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(&hdr->full[i], 33);  // producer lane 0 + 32 cp.async arrivals
-      mbar_init(&hdr->empty[i], kConsumerWarps);
+      mbar_init(&hdr->empty[i], KVC);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&hdr->qfull[i], 1);
-      mbar_init(&hdr->qempty[i], kConsumerWarps);
+      mbar_init(&hdr->qempty[i], KVC);
     }
+    hdr->nmerge = 0;
     fence_mbar_init();
   }
   __syncthreads();
-  if (threadIdx.x >= kConsumerWarps * 32)
+  if (threadIdx.x >= KVC * 32)
     decode_producer<D, LAYOUT>(p, hdr, qbuf, rbuf, stg);
   else
     decode_consumer<D, NT, LAYOUT, KVC>(p, hdr, qbuf, rbuf, stg);
-}
-
-// ------------------------------------------------------------------- combine --
-// One warp per (segment, q head): lanes load the (m, l) of up to 32 partials
-// at once, reduce the log-sum-exp weights with shuffles, then accumulate the
-// weighted partial rows (each lane owns D/32 dims) and write the output row.
-template <int D>
-__global__ void __launch_bounds__(256) decode_combine_kernel(
-    const DecodeParams p, void* out, int out_dtype, int64_t out_seq_stride,
-    int64_t out_head_stride) {
-  const int B = p.num_seqs;
-  const int hg = p.kvc * p.G;
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t nsegs = (int64_t)p.ngroups * B;
-  if (gw >= nsegs * hg) return;
-  const int e = (int)(gw / hg), hl = (int)(gw % hg);
-  const int kg = e / B, s = e % B;
-
-  long long pre = 0, tot = 0;
-  for (int b = lane; b < B; b += 32) {
-    const int n = nchunks_of(seq_len_of(p, b));
-    tot += n;
-    if (b < s) pre += n;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    pre += __shfl_xor_sync(0xffffffffu, pre, o);
-    tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  }
-  const int n_s = nchunks_of(seq_len_of(p, s));
-  const int64_t T = tot * p.ngroups;
-  const int64_t P0 = (int64_t)kg * tot + pre;
-  const int64_t NC = p.num_ctas;
-
-  constexpr int DPL = (D + 31) / 32;  // dims per lane
-  float o[DPL];
-#pragma unroll
-  for (int i = 0; i < DPL; ++i) o[i] = 0.f;
-  float Lsum = 0.f;
-  if (n_s > 0) {
-    const int64_t c_first = cta_of_unit(P0, T, NC);
-    const int64_t c_last = cta_of_unit(P0 + n_s - 1, T, NC);
-    const int np = (int)(c_last - c_first + 1) * p.wpk;
-    // pass 1: running max over all partials, 32 at a time
-    float M = -INFINITY;
-    for (int i0 = 0; i0 < np; i0 += 32) {
-      const int i = i0 + lane;
-      float m = -INFINITY;
-      if (i < np) {
-        const int64_t c = c_first + i / p.wpk;
-        const int64_t a = cta_start(c, T, NC), b2 = cta_start(c + 1, T, NC);
-        if (a < b2 && b2 > P0 && a < P0 + n_s) {
-          const int64_t row = ((c + e) * p.wpk + i % p.wpk) * hg + hl;
-          m = p.part_ml[row * 2];
-        }
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-      M = fmaxf(M, m);
-    }
-    // pass 2: weights and weighted rows
-    if (M != -INFINITY) {
-      for (int i0 = 0; i0 < np; i0 += 32) {
-        const int i = i0 + lane;
-        float wgt = 0.f, lw = 0.f;
-        int64_t row = -1;
-        if (i < np) {
-          const int64_t c = c_first + i / p.wpk;
-          const int64_t a = cta_start(c, T, NC), b2 = cta_start(c + 1, T, NC);
-          if (a < b2 && b2 > P0 && a < P0 + n_s) {
-            row = ((c + e) * p.wpk + i % p.wpk) * hg + hl;
-            wgt = exp2f(p.part_ml[row * 2] - M);
-            lw = wgt * p.part_ml[row * 2 + 1];
-          }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
-        Lsum += lw;
-        const int cnt = min(32, np - i0);
-        for (int k = 0; k < cnt; ++k) {
-          const float wk = __shfl_sync(0xffffffffu, wgt, k);
-          const int64_t rk = __shfl_sync(0xffffffffu, row, k);
-          if (rk >= 0) {
-            const float* src = p.part_acc + rk * D;
-#pragma unroll
-            for (int dd = 0; dd < DPL; ++dd) {
-              const int d = lane + 32 * dd;
-              if (d < D) o[dd] += wk * src[d];
-            }
-          }
-        }
-      }
-    }
-  }
-  const float inv = (Lsum > 0.f) ? 1.f / Lsum : 0.f;
-  const int64_t obase = (int64_t)s * out_seq_stride + (int64_t)(kg * hg + hl) * out_head_stride;
-#pragma unroll
-  for (int dd = 0; dd < DPL; ++dd) {
-    const int d = lane + 32 * dd;
-    if (d < D) {
-      const float v = o[dd] * inv;
-      if (out_dtype == 2)
-        reinterpret_cast<float*>(out)[obase + d] = v;
-      else if (out_dtype == 1)
-        reinterpret_cast<__nv_bfloat16*>(out)[obase + d] = __float2bfloat16_rn(v);
-      else
-        reinterpret_cast<__half*>(out)[obase + d] = __float2half_rn(v);
-    }
-  }
 }
 
 }  // namespace slmt

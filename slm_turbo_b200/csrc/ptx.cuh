@@ -103,6 +103,17 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
                : "memory");
 }
 
+// 16-byte cp.async global -> shared through L2 only (.cg: coherent with
+// stores other CTAs made during the kernel).
+__device__ __forceinline__ void cp_async16_cg(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // Arrive on `bar` once all earlier cp.async of this thread landed; the
 // barrier's expected count already includes this arrival (.noinc).
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {

@@ -168,3 +168,24 @@ def test_paged_decode_c3_full_size():
                                      case["seq_lens"].to(dev))
     assert kd.read_device_errors(dev) == 0
     assert_close(got.cpu().numpy(), want, what="C3")
+
+
+def test_paged_decode_empty_runs_and_many_short_sequences():
+    """Runs of 32+ empty sequences between non-empty ones, and a batch of
+    300 short sequences (many segments per CTA: exercises the producer's
+    next-segment and page-window prefetch)."""
+    kd = _kd()
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(31)
+    cases = [
+        [0] * 40 + [50] + [0] * 5 + [3000] + [0] * 33 + [17] + [0] * 3,
+        torch.randint(0, 90, (300,), generator=g).tolist(),
+    ]
+    for lengths in cases:
+        case = ragged_paged_case(lengths, d=128, kv=8, hq=32, seed=len(lengths))
+        cache_cpu, cache_gpu = _store_both(case)
+        want = oracle.paged_decode(case["q"], cache_cpu, case["block_tables"], case["seq_lens"], 16, 8)
+        got = kd.kv_decode_paged_batched(case["q"].to(dev), cache_gpu, case["block_tables"].to(dev),
+                                         case["seq_lens"].to(dev))
+        assert kd.read_device_errors(dev) == 0
+        assert_close(got.cpu().numpy(), want, what=f"B={len(lengths)}")
