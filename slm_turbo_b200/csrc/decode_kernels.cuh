@@ -116,10 +116,19 @@ __device__ __forceinline__ void load_bytes(const uint8_t* ptr, uint32_t* w) {
 // row; one 32-bit word feeds two k-steps (low nibbles of bytes 0/2 and 1/3
 // pair up in one f16x2), a trailing 2-byte word (D = 80) feeds one.
 template <int D>
+__device__ __forceinline__ int kword_byte(int r, int u) {
+  constexpr int QB = D / 8;
+  // D = 128: a lane's 16 bytes are [8r, 8r+8) and [32+8r, 40+8r), so each of
+  // its two 8-byte loads covers 32 contiguous bytes across the 4 lanes of a row
+  if constexpr (QB == 16) return 32 * (u >> 1) + 8 * r + 4 * (u & 1);
+  return r * QB + 4 * u;
+}
+
+template <int D>
 __device__ __forceinline__ int qk_dim(int s, int slot, int r) {
   constexpr int QB = D / 8;
   const int u = s >> 1, e = s & 1;
-  const int base = r * QB + 4 * u;
+  const int base = kword_byte<D>(r, u);
   const int nib = (slot >> 1) & 1;
   int byte;
   if (4 * u + 4 <= QB)
@@ -130,25 +139,38 @@ __device__ __forceinline__ int qk_dim(int s, int slot, int r) {
 }
 
 // Shared-memory addresses of token row t (0..31) of kv head j in a stage.
-// `base` already holds the warp's kv-head offset, so every row address is
-// base + immediate.
+// `base` already holds the warp's kv-head offset; paged rows are KVC*(D+8)
+// bytes apart, contiguous layouts hold D/2-byte K and V rows.
 template <int D, int LAYOUT, int KVC>
 struct StageView {
+  static constexpr int kRow = (LAYOUT == LAYOUT_PAGED) ? KVC * (D + 8) : D / 2;  // row stride
+  // byte distance of rows t+8 / t+16 from row t
+  static constexpr int d8 = 8 * kRow;
+  static constexpr int d16 = 16 * kRow;
+  static constexpr int r8 = (LAYOUT == LAYOUT_PAGED) ? d8 : 8 * KVC * 8;
+  static constexpr int r16 = (LAYOUT == LAYOUT_PAGED) ? d16 : 16 * KVC * 8;
   const uint8_t* base;  // paged: st + j*(D+8); contiguous: st + j*32*D
   const uint8_t* rul;   // contiguous per-token rulers: st + KVC*32*D + j*8
   __device__ __forceinline__ const uint8_t* k(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return base + t * KVC * (D + 8);
+    if (LAYOUT == LAYOUT_PAGED) return base + t * kRow;
     return base + t * (D / 2);
   }
   __device__ __forceinline__ const uint8_t* v(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return base + t * KVC * (D + 8) + D / 2;
+    if (LAYOUT == LAYOUT_PAGED) return base + t * kRow + D / 2;
     return base + (kChunkTokens / 2) * D + t * (D / 2);
   }
   __device__ __forceinline__ const uint8_t* rulers(int t) const {
-    if (LAYOUT == LAYOUT_PAGED) return base + t * KVC * (D + 8) + D;
+    if (LAYOUT == LAYOUT_PAGED) return base + t * kRow + D;
     return rul + t * KVC * 8;
   }
 };
+
+// Stage row (token) behind fragment row i of a consumer's tiles.
+template <int D, int LAYOUT, int KVC>
+__device__ __forceinline__ int stage_tok(int i) {
+  if constexpr (LAYOUT == LAYOUT_PAGED) return tok_of(i);
+  return i;
+}
 
 // ------------------------------------------------------------------ producer --
 // Page ids of 32 consecutive 16-token tiles of sequence s, one per lane.
@@ -625,14 +647,13 @@ __device__ void merge_segment(const DecodeParams& p, const MergeJob& job, float*
 }
 
 // ------------------------------------------------------------------ consumer --
-// K codes enter QK with the magic-number bias left in: the low nibble as
-// fp16 1024+c, the high nibble as 64+c (exponent 0x54, nibble in mantissa
-// bits 4..7).  sum_d q_d*(bias_d + c_d) = q.c + sum_d q_d*bias_d, and the
-// second term (one number per head) starts the accumulator negated, so the
-// tensor core returns q.c directly and no f16x2 subtract is spent per code.
-__device__ __forceinline__ uint32_t kcodes_lo(uint32_t w) { return lop_and_or(w, 0x000F000Fu, 0x64006400u); }
-__device__ __forceinline__ uint32_t kcodes_hi(uint32_t w) { return lop_and_or(w, 0x00F000F0u, 0x54005400u); }
-
+// Both operands that carry codes keep the magic-number bias (low nibble
+// 1024+c, high nibble 64+c).  QK: sum_d q_d*(bias_d + c_d) = q.c +
+// sum_d q_d*bias_d, and the second term (one number per head) starts the
+// accumulator negated.  PV: sum_t P'_t*(bias_d + c_td) = P'.c_d +
+// bias_d*sum_t P'_t, and sum_t P'_t comes from the same P' against a ones
+// tile, subtracted when the segment's rows are finalised.  No f16x2 op is
+// spent per code.
 // Per-thread state of one consumer warp (head columns 2r, 2r+1 of each
 // 8-head n-tile; output rows = head dims 2*(g*D/16 + mt) + {0, 1}).
 template <int D, int NT>
@@ -641,7 +662,8 @@ struct WarpState {
   uint4 qf[NT][(D / 8 + 3) / 4];  // q B-fragments: k-steps 2u (x, y) and 2u+1 (z, w)
   float qs[NT][2];         // log2e*scale * (sum q (per-token) | sum q'*zero (per-channel))
   float qb[NT][2];         // QK accumulator bias: sum_d q_d * (1024 | 64)
-  float acc[KS][NT][4];
+  float acc[KS][NT][4];     // O^T on biased V codes: rows g hold 1024 + c, rows g+8 hold 64 + c
+  float ps[NT][2];          // sum over tokens of P' per head column, to take the V bias off
   float m[NT][2], l[NT][2], vs[NT][2];
 };
 
@@ -658,44 +680,59 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   constexpr int VALIGN = (VB % 8 == 0) ? 8 : ((VB % 4 == 0) ? 4 : 1);
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, r = lane & 3;
+  // stage rows (tokens) behind this lane's fragment rows: QK / scores use
+  // rows g and g+8 of each tile, PV uses rows 2r, 2r+1, 2r+8, 2r+9
+  using SV = StageView<D, LAYOUT, KVC>;
+  const int gt = stage_tok<D, LAYOUT, KVC>(g);
+  const uint8_t* krow = sv.k(gt);  // + a*d16 + h*d8 -> row 16a + g + 8h
+  const uint8_t* rrow = sv.rulers(gt);
+  const uint8_t* vrow0 = sv.v(stage_tok<D, LAYOUT, KVC>(2 * r));
+  const uint8_t* vrow1 = sv.v(stage_tok<D, LAYOUT, KVC>(2 * r + 1));
 
-  // ---- QK on biased codes, tile by tile; even/odd k-steps in two chains ----
+  // ---- QK on biased codes, tile by tile (one accumulator chain per tile:
+  // a second chain per tile costs registers the kernel does not have) ----
   float sacc[2][NT][4];
 #pragma unroll
   for (int a = 0; a < 2; ++a) {
-    float c[NT][4], c2[NT][4];
+    float c[NT][4];
     asm volatile("" ::: "memory");  // keep the two tiles' loads from being hoisted together
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       c[nt][0] = c[nt][2] = -w.qb[nt][0];
       c[nt][1] = c[nt][3] = -w.qb[nt][1];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) c2[nt][i] = 0.f;
     }
     uint32_t ka[QW], kb[QW];
-    load_bytes<QB, QALIGN>(sv.k(16 * a + g) + r * QB, ka);
-    load_bytes<QB, QALIGN>(sv.k(16 * a + g + 8) + r * QB, kb);
+    const uint8_t* k0 = krow + a * SV::d16;
+    if constexpr (QB == 16) {
+      load_bytes<8, 8>(k0 + 8 * r, ka);
+      load_bytes<8, 8>(k0 + 32 + 8 * r, ka + 2);
+      load_bytes<8, 8>(k0 + SV::d8 + 8 * r, kb);
+      load_bytes<8, 8>(k0 + SV::d8 + 32 + 8 * r, kb + 2);
+    } else {
+      load_bytes<QB, QALIGN>(k0 + r * QB, ka);
+      load_bytes<QB, QALIGN>(k0 + SV::d8 + r * QB, kb);
+    }
 #pragma unroll
     for (int u = 0; u < QW; ++u) {
       uint4 qf[NT];  // B-fragments of k-steps 2u (x, y) and 2u+1 (z, w)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) qf[nt] = w.qf[nt][u];
       if (4 * u + 4 <= QB) {
-        uint32_t a0 = kcodes_lo(ka[u]), a1 = kcodes_lo(kb[u]);
-        uint32_t a2 = kcodes_hi(ka[u]), a3 = kcodes_hi(kb[u]);
+        uint32_t a0 = codes_lo_biased(ka[u]), a1 = codes_lo_biased(kb[u]);
+        uint32_t a2 = codes_hi_biased(ka[u]), a3 = codes_hi_biased(kb[u]);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
         const uint32_t sa = ka[u] >> 8, sb = kb[u] >> 8;
-        a0 = kcodes_lo(sa);
-        a1 = kcodes_lo(sb);
-        a2 = kcodes_hi(sa);
-        a3 = kcodes_hi(sb);
+        a0 = codes_lo_biased(sa);
+        a1 = codes_lo_biased(sb);
+        a2 = codes_hi_biased(sa);
+        a3 = codes_hi_biased(sb);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_16816(c2[nt], a0, a1, a2, a3, qf[nt].z, qf[nt].w);
+        for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].z, qf[nt].w);
       } else {
         const uint32_t sa = __byte_perm(ka[u], 0u, 0x3120), sb = __byte_perm(kb[u], 0u, 0x3120);
-        const uint32_t a0 = kcodes_lo(sa), a1 = kcodes_lo(sb);
-        const uint32_t a2 = kcodes_hi(sa), a3 = kcodes_hi(sb);
+        const uint32_t a0 = codes_lo_biased(sa), a1 = codes_lo_biased(sb);
+        const uint32_t a2 = codes_hi_biased(sa), a3 = codes_hi_biased(sb);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
       }
@@ -703,24 +740,24 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sacc[a][nt][i] = c[nt][i] + c2[nt][i];
+      for (int i = 0; i < 4; ++i) sacc[a][nt][i] = c[nt][i];
   }
 
   // ---- per-token rulers (k_min, k_step | v_min, v_step) are read from shared
   // memory where they are used, to keep registers free ----
   auto ruler_k = [&](int a, int h) -> float2 {
     if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(p.use_quant ? -1.f : 0.f, 1.f);
-    return __half22float2(*reinterpret_cast<const __half2*>(sv.rulers(16 * a + g + 8 * h)));
+    return __half22float2(*reinterpret_cast<const __half2*>(rrow + a * SV::r16 + h * SV::r8));
   };
   auto ruler_v = [&](int a, int h) -> float2 {
     if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(0.f, 1.f);
-    return __half22float2(*reinterpret_cast<const __half2*>(sv.rulers(16 * a + g + 8 * h) + 4));
+    return __half22float2(*reinterpret_cast<const __half2*>(rrow + a * SV::r16 + h * SV::r8 + 4));
   };
   bool val[2][2];
 #pragma unroll
   for (int a = 0; a < 2; ++a)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * a + g + 8 * h) < nvalid;
+    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * a + gt + 8 * h) < nvalid;
 
   // ---- scores + online softmax (log2 domain, lazy rescale) ----
   const float sl2 = p.scale_log2;
@@ -771,6 +808,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
         w.m[nt][e] = mn;
         w.l[nt][e] *= al;
         w.vs[nt][e] *= al;
+        w.ps[nt][e] *= al;
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
           w.acc[mt][nt][e] *= al;
@@ -805,15 +843,22 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     }
   }
 
-  // ---- PV on raw codes: O^T[dims x heads] += V^T . P'^T, one k-step per tile ----
-  // thread (g, r) needs tokens 16a + {2r, 2r+1, 2r+8, 2r+9}, bytes [g*VB, +VB)
+  // ---- PV on biased codes: O^T[dims x heads] += (V^T + bias) . P'^T, one
+  // k-step per tile; the same P' against a ones tile gives sum_t P'_t per
+  // head, exactly as the tensor core sums it, to take the bias off later ----
+  // thread (g, r) needs fragment rows 16a + {2r, 2r+1, 2r+8, 2r+9} (tokens
+  // through tok_of), bytes [g*VB, +VB)
+  constexpr uint32_t kOnes = 0x3C003C00u;  // fp16x2 (1, 1)
 #pragma unroll
   for (int a = 0; a < 2; ++a) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      mma_16816_rows0(w.ps[nt][0], w.ps[nt][1], kOnes, kOnes, kOnes, kOnes, pb[a][nt][0], pb[a][nt][1]);
     uint32_t vw[4][VW];
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r) + g * VB, vw[0]);
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 1) + g * VB, vw[1]);
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 8) + g * VB, vw[2]);
-    load_bytes<VB, VALIGN>(sv.v(16 * a + 2 * r + 9) + g * VB, vw[3]);
+    load_bytes<VB, VALIGN>(vrow0 + a * SV::d16 + g * VB, vw[0]);
+    load_bytes<VB, VALIGN>(vrow1 + a * SV::d16 + g * VB, vw[1]);
+    load_bytes<VB, VALIGN>(vrow0 + a * SV::d16 + SV::d8 + g * VB, vw[2]);
+    load_bytes<VB, VALIGN>(vrow1 + a * SV::d16 + SV::d8 + g * VB, vw[3]);
     if (a == 1 && release) {  // every shared-memory read of the stage is done: release it
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar);
@@ -830,8 +875,8 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
         if (mt < KS) {
           const uint32_t w1 = (k == 0) ? x : (k == 1) ? (x >> 8) : (k == 2) ? y : (y >> 8);
           const uint32_t w2 = (k == 0) ? x2 : (k == 1) ? (x2 >> 8) : (k == 2) ? y2 : (y2 >> 8);
-          const uint32_t a0 = codes_lo(w1), a1 = codes_hi(w1);
-          const uint32_t a2 = codes_lo(w2), a3 = codes_hi(w2);
+          const uint32_t a0 = codes_lo_biased(w1), a1 = codes_hi_biased(w1);
+          const uint32_t a2 = codes_lo_biased(w2), a3 = codes_hi_biased(w2);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) mma_16816(w.acc[mt][nt], a0, a1, a2, a3, pb[a][nt][0], pb[a][nt][1]);
         }
@@ -929,6 +974,8 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
         w.l[nt][0] = w.l[nt][1] = 0.f;
         w.vs[nt][0] = w.vs[nt][1] = 0.f;
 #pragma unroll
+        for (int i = 0; i < 2; ++i) w.ps[nt][i] = 0.f;
+#pragma unroll
         for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
           for (int i = 0; i < 4; ++i) w.acc[mt][nt][i] = 0.f;
@@ -997,8 +1044,8 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
             float* dst = p.part_acc + row * D + 2 * g * VB;
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
-              float o0 = w.acc[mt][nt][e] + vsum;
-              float o1 = w.acc[mt][nt][e + 2] + vsum;
+              float o0 = fmaf(-1024.f, w.ps[nt][e], w.acc[mt][nt][e]) + vsum;
+              float o1 = fmaf(-64.f, w.ps[nt][e], w.acc[mt][nt][e + 2]) + vsum;
               if (LAYOUT == LAYOUT_PER_CHANNEL && p.use_quant) {
                 const int d0 = 2 * (g * VB + mt);
                 o0 = __half2float(vsc[d0]) * (o0 - __half2float(vze[d0]) * lsum);

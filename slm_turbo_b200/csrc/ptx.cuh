@@ -135,6 +135,19 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// As mma_16816 for a tile whose C rows g and g+8 are known to be equal (an A
+// tile of identical rows): only rows g are kept (c0, c1); rows g+8 land in
+// temporaries that die here.
+__device__ __forceinline__ void mma_16816_rows0(float& c0, float& c1, uint32_t a0, uint32_t a1,
+                                                uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  float d2 __attribute__((unused)), d3 __attribute__((unused));
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%10,%10};"
+      : "+f"(c0), "+f"(c1), "=f"(d2), "=f"(d3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // Transpose of an 8x8 b16 matrix held one row-pair per thread.
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
@@ -146,11 +159,12 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
 
 // ------------------------------------------------------ 4-bit -> fp16 codes --
 // IEEE fp16 1024 is 0x6400 and has ulp 1 on [1024, 2048), so OR-ing a nibble
-// into the low mantissa bits gives 1024+c exactly; OR-ing a nibble that sits
-// in bits 4..7 gives 1024+16c.  One LOP3 builds two such halves, one f16x2
-// subtract (or fma by 1/16, -64) makes the integers 0..15 exact.  (The
-// magic-number int4 -> fp16 conversion from the mixed-input GEMM literature,
-// e.g. Kim et al. 2022, "Who Says Elephants Can't Run".)
+// into the low mantissa bits gives 1024+c exactly; fp16 64 is 0x5400 and has
+// ulp 1/16 on [64, 128), so OR-ing a nibble that sits in bits 4..7 gives
+// 64+c exactly.  One LOP3 builds two such halves.  (The magic-number int4 ->
+// fp16 conversion of the mixed-input GEMM literature, e.g. Kim et al. 2022,
+// "Who Says Elephants Can't Run".)  The bias (1024 or 64 per nibble) is left
+// in: the kernels take it off once per dot product instead of once per code.
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask,
                                                uint32_t orv) {
   uint32_t d;
@@ -158,21 +172,14 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask,
   return d;
 }
 
-// halves = (low nibble of byte 0, low nibble of byte 2) as exact fp16
-__device__ __forceinline__ uint32_t codes_lo(uint32_t w) {
-  uint32_t t = lop_and_or(w, 0x000F000Fu, 0x64006400u), d;
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(d) : "r"(t), "r"(0x64006400u));
-  return d;
+// halves = 1024 + (low nibble of byte 0, low nibble of byte 2)
+__device__ __forceinline__ uint32_t codes_lo_biased(uint32_t w) {
+  return lop_and_or(w, 0x000F000Fu, 0x64006400u);
 }
 
-// halves = (high nibble of byte 0, high nibble of byte 2) as exact fp16
-__device__ __forceinline__ uint32_t codes_hi(uint32_t w) {
-  uint32_t t = lop_and_or(w, 0x00F000F0u, 0x64006400u), d;
-  // (1024 + 16c) * (1/16) + (-64) = c, one rounding, exact.
-  asm("fma.rn.f16x2 %0, %1, %2, %3;"
-      : "=r"(d)
-      : "r"(t), "r"(0x2C002C00u), "r"(0xD400D400u));
-  return d;
+// halves = 64 + (high nibble of byte 0, high nibble of byte 2)
+__device__ __forceinline__ uint32_t codes_hi_biased(uint32_t w) {
+  return lop_and_or(w, 0x00F000F0u, 0x54005400u);
 }
 
 __device__ __forceinline__ float exp2_approx(float x) {
