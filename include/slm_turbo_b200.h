@@ -53,6 +53,8 @@ extern "C" {
 #define SLMT_ERR_UNSUPPORTED (-7) /* valid but unsupported (e.g. H/KV > 16)   */
 #define SLMT_ERR_CUDA (-8)        /* CUDA runtime error at launch             */
 #define SLMT_ERR_BLOCK (-9)       /* BLOCK_N / BLOCK_M value rejected         */
+#define SLMT_ERR_SCRATCH_LIMIT (-10) /* request needs more than the static    */
+                                    /* scratch of slmt_paged_decode_noalloc  */
 
 /* ---- device error word bits (OR-ed into *err_flag by the kernels) -------- */
 #define SLMT_DEVERR_BLOCK_ID 1u /* block-table entry outside [0, num_blocks)    */
@@ -219,6 +221,49 @@ int slmt_per_channel_append(const void* x, int x_dtype, int64_t x_head_stride,
                             const uint16_t* scale, const uint16_t* zero,
                             uint8_t* packed, int64_t s_cap, int64_t pos,
                             void* stream);
+
+/*
+ * slmt_paged_decode with no workspace argument: its split-K scratch is a
+ * static device array of SLMT_NOALLOC_SCRATCH_BYTES inside this library, so
+ * the call allocates no device memory (no cudaMalloc/cudaFree, no allocating
+ * library routine).  It is for callers that cannot allocate when they decode
+ * -- an engine that gave all of HBM to its page pool and activation arena up
+ * front, or a plugin host that offers the op no allocator -- and so cannot
+ * pass slmt_paged_decode a workspace.  No counterpart in the reference (its
+ * single-request decode needs no scratch).  Every other argument, the
+ * results and the statuses are those of slmt_paged_decode.
+ * Limit: a request whose worst-case scratch (slmt_decode_workspace_bytes of
+ * num_seqs, num_q_heads, num_kv_heads, head_dim) exceeds the array returns
+ * SLMT_ERR_SCRATCH_LIMIT before anything is launched; 8 MiB covers e.g. 64
+ * sequences at 32 query heads x 128 dims on a 148-SM device.
+ * Zero state: the array starts zero-filled when the module loads.  Its first
+ * (kv groups x num_seqs) int32 words are arrival counters that must be zero
+ * when a launch starts; each launch that completes without a device error
+ * bit leaves them at zero.  After a call that set a bit in *err_flag, pass
+ * reset_scratch != 0 on the next call: that zeroes the counters with
+ * cudaMemsetAsync on `stream` before the launch (0 skips it).
+ * Set-up: the first call on each device (with that device current) looks up
+ * the array's address with cudaGetSymbolAddress, which may load the module,
+ * and the first decode call configures the kernel; make that first call
+ * before any stream capture begins.
+ * Concurrency: all calls on one device share the one array, so two calls
+ * whose executions overlap (different streams, or different host threads)
+ * race on it and give wrong results; order them on one stream or with
+ * events.
+ */
+#define SLMT_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+int slmt_paged_decode_noalloc(const void* q, int q_dtype, int64_t q_seq_stride,
+                              int64_t q_head_stride, const uint8_t* kv_cache,
+                              int64_t num_blocks, int64_t block_size,
+                              int64_t num_kv_heads, int64_t head_dim,
+                              const void* block_tables, int bt_dtype,
+                              int64_t bt_seq_stride, int64_t max_blocks_per_seq,
+                              const int32_t* seq_lens, int64_t seq_len_scalar,
+                              int64_t max_seq_len_hint, int64_t num_seqs,
+                              int64_t num_q_heads, float sm_scale, void* out,
+                              int out_dtype, int64_t out_seq_stride,
+                              int64_t out_head_stride, int reset_scratch,
+                              int32_t* err_flag, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

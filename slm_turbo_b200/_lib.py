@@ -30,6 +30,9 @@ SIGNATURES = {
     "slmt_paged_decode": (_i32, [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i64, _i64,
                                  _vp, _i64, _i64, _i64, _i64, _f32, _vp, _i32, _i64, _i64, _vp, _i64, _vp,
                                  _vp]),
+    "slmt_paged_decode_noalloc": (_i32, [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i64,
+                                         _i64, _vp, _i64, _i64, _i64, _i64, _f32, _vp, _i32, _i64, _i64, _i32,
+                                         _vp, _vp]),
     "slmt_per_channel_decode": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64,
                                        _i32, _vp, _i64, _i32, _i64, _i64, _i64, _i64, _f32, _vp, _i32, _i64,
                                        _i64, _vp, _i64, _vp, _vp]),

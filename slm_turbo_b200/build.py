@@ -20,7 +20,7 @@ CSRC = HERE / "csrc"
 INCLUDE = ROOT / "include"
 LIB_NAME = "libslm_turbo_b200.so"
 LIB_PATH = HERE / LIB_NAME
-SOURCES = ["decode.cu", "store.cu"]
+SOURCES = ["decode.cu", "store.cu", "decode_noalloc.cu"]
 HEADERS = ["ptx.cuh", "decode_common.cuh", "decode_kernels.cuh", "internal.h"]
 
 NVCC_FLAGS = [

@@ -325,6 +325,9 @@ extern "C" const char* slmt_status_string(int status) {
       return "CUDA runtime error";
     case SLMT_ERR_BLOCK:
       return "BLOCK_N / BLOCK_M rejected";
+    case SLMT_ERR_SCRATCH_LIMIT:
+      return "request needs more scratch than slmt_paged_decode_noalloc's static array "
+             "(SLMT_NOALLOC_SCRATCH_BYTES)";
     default:
       return "unknown status";
   }
