@@ -161,19 +161,27 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ profiles
-def profiled_traffic():
-    """dram read+write bytes per decode launch from the committed ncu summary
-    (a `traffic_bytes_per_launch:` line), or None."""
+def profiled_traffic(dec_bytes):
+    """DRAM read+write bytes per decode launch from the committed ncu summary
+    (`traffic_bytes_per_launch:` of a capture whose workload moved
+    `traffic_algorithmic_bytes:`), scaled to this workload's algorithmic
+    bytes (traffic grows in proportion to them); None if absent."""
     p = ROOT / "profiles" / "decode_splitk_c3.txt"
     if not p.exists():
         return None
+    vals = {}
     for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
-                return int(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+        for key in ("traffic_bytes_per_launch:", "traffic_algorithmic_bytes:"):
+            if line.startswith(key):
+                try:
+                    vals[key] = int(line.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
+    t = vals.get("traffic_bytes_per_launch:")
+    base = vals.get("traffic_algorithmic_bytes:")
+    if t is None:
+        return None
+    return int(round(t * dec_bytes / base)) if base else t
 
 
 def measured_peak():
@@ -378,8 +386,9 @@ def run_ours(args):
     # ---- end to end through the public API with pinned host buffers ----
     # Each step's inputs (q, new K/V, slots, lengths) travel in ONE pinned
     # host -> device copy and its fp32 output in one device -> host copy, on
-    # a copy stream, double-buffered: the copies of steps t+1 (in) and t-1
-    # (out) run while step t computes, as a serving loop would run them.
+    # their own copy streams, double-buffered: the input copy of step t+1 and
+    # the output copy of step t-1 run while step t computes, as a serving
+    # loop would run them.
     h_parts = [q.cpu(), k_new.cpu(), v_new.cpu(), step_slots(w), w["seq_lens1"]]
     offs, o = [], 0
     for t in h_parts:
@@ -403,21 +412,29 @@ def run_ours(args):
     d_out = [torch.empty(B, HQ, D, dtype=torch.float32, device=dev) for _ in range(2)]
     h_out = [torch.empty(B, HQ, D, dtype=torch.float32).pin_memory() for _ in range(2)]
     d2h = h_out[0].numel() * h_out[0].element_size()
-    cstream = torch.cuda.Stream(dev)
+    h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]     # inputs of slot landed
     ev_done = [torch.cuda.Event() for _ in range(2)]   # compute of slot finished
     ev_out = [torch.cuda.Event() for _ in range(2)]    # output of slot copied out
 
     def e2e_run(n):
         cs = torch.cuda.current_stream(dev)  # compute stream (the capture stream under a graph)
-        cstream.wait_stream(cs)
+        h2d_stream.wait_stream(cs)
+        d2h_stream.wait_stream(cs)
+
+        def copy_in(i):
+            sl = i & 1
+            with torch.cuda.stream(h2d_stream):
+                if i >= 2:
+                    h2d_stream.wait_event(ev_done[sl])  # slot's previous inputs consumed
+                d_in[sl].copy_(h_in, non_blocking=True)
+                ev_in[sl].record(h2d_stream)
+
+        copy_in(0)
         for i in range(n):
             sl = i & 1
-            with torch.cuda.stream(cstream):
-                if i >= 2:
-                    cstream.wait_event(ev_done[sl])  # slot's previous inputs consumed
-                d_in[sl].copy_(h_in, non_blocking=True)
-                ev_in[sl].record(cstream)
+            if i + 1 < n:
+                copy_in(i + 1)  # prefetch: overlaps step i's compute
             cs.wait_event(ev_in[sl])
             if i >= 2:
                 cs.wait_event(ev_out[sl])  # slot's previous output read out
@@ -425,11 +442,12 @@ def run_ours(args):
             kd.kv_quantize_store(dk, dv, cache, dslots, BS)
             kd.kv_decode_paged_batched(dq, cache, bt_d, dsl, out=d_out[sl], max_seq_len=maxlen)
             ev_done[sl].record(cs)
-            with torch.cuda.stream(cstream):
-                cstream.wait_event(ev_done[sl])
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(ev_done[sl])
                 h_out[sl].copy_(d_out[sl], non_blocking=True)
-                ev_out[sl].record(cstream)
-        cs.wait_stream(cstream)
+                ev_out[sl].record(d2h_stream)
+        cs.wait_stream(h2d_stream)
+        cs.wait_stream(d2h_stream)
 
     # The steps are replayed from a CUDA graph of E2E_GRAPH_STEPS pipelined
     # steps (the public API calls captured once), as a serving engine runs
@@ -480,14 +498,14 @@ def run_ours(args):
         "decode_us": dec_ms * 1e3, "decode_hbm_gbs": achieved,
         "hbm_pct_of_8tbs": 100.0 * achieved / NOMINAL_HBM_GBS,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": profiled_traffic(),
+                     "frac": achieved / peak, "traffic": profiled_traffic(dec_bytes),
                      "kernel": "decode_splitk_kernel<128,1,PAGED,8> (partials merged inside the launch)",
                      "algorithmic_bytes_per_launch": dec_bytes, "peak_source": peak_src},
         "e2e": {"value": total_seqs / (e2e_ms * 1e-3),
                 "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "mode": f"public API captured as a CUDA graph of {E2E_GRAPH_STEPS} steps; per step one "
-                        "pinned H2D of the inputs and one D2H of the fp32 output on a copy stream, "
-                        "double-buffered against the compute",
+                        "pinned H2D of the inputs and one D2H of the fp32 output, each on its own copy "
+                        "stream, double-buffered against the compute",
                 "ms_per_step": e2e_ms},
         "gpu_launches": 2 * args.steps,  # kv_store_kernel + decode_splitk_kernel per step
         "clocks": clk.summary(),

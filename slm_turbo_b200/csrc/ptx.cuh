@@ -77,7 +77,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 
 // ------------------------------------------------------------ async copies --
 // 1-D bulk copy global -> shared (TMA unit), completes `bytes` of tx on `bar`.
-// src and dst 16-byte aligned, bytes a multiple of 16.  No multicast.
+// src and dst 16-byte aligned, bytes a multiple of 16; the source is always
+// this GPU's own memory and the destination this CTA's shared memory.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src,
                                          uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
