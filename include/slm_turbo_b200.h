@@ -74,10 +74,12 @@ int slmt_device_sm_count(int device);
 /*
  * Bytes of split-K scratch the decode entry points need for `num_seqs`
  * sequences (pseudo-sequences for prefill) on `device`; negative on error.
- * The scratch must be zero-filled before its first use (it holds per-segment
- * arrival counters, which every completed call leaves at zero again), must
- * be 256-byte aligned, and must not be shared by calls that overlap on the
- * GPU.  If a call reports a device error, zero it again before reuse.
+ * The first workspace_bytes/64 bytes (rounded up to 256) of the scratch hold
+ * per-segment arrival counters: they must be zero before the first use, and
+ * every completed call leaves them at zero again, so one scratch serves calls
+ * of any batch size it is large enough for (pass the same workspace_bytes
+ * each time).  It must be 256-byte aligned and must not be shared by calls
+ * that overlap on the GPU.  If a call reports a device error, zero it again.
  */
 int64_t slmt_decode_workspace_bytes(int64_t num_seqs, int64_t num_q_heads,
                                     int64_t num_kv_heads, int64_t head_dim,
@@ -237,9 +239,8 @@ int slmt_per_channel_append(const void* x, int x_dtype, int64_t x_head_stride,
  * SLMT_ERR_SCRATCH_LIMIT before anything is launched; 8 MiB covers e.g. 64
  * sequences at 32 query heads x 128 dims on a 148-SM device.
  * Zero state: the array starts zero-filled when the module loads.  Its first
- * (kv groups x num_seqs) int32 words are arrival counters that must be zero
- * when a launch starts; each launch that completes without a device error
- * bit leaves them at zero.  After a call that set a bit in *err_flag, pass
+ * 1/64 holds arrival counters that must be zero when a launch starts; each
+ * launch that completes without a device error bit leaves them at zero.  After a call that set a bit in *err_flag, pass
  * reset_scratch != 0 on the next call: that zeroes the counters with
  * cudaMemsetAsync on `stream` before the launch (0 skips it).
  * Set-up: the first call on each device (with that device current) looks up

@@ -131,11 +131,19 @@ int64_t workspace_floats(int64_t slots, const Geometry& g, int D) {
 }
 
 // Scratch layout: [segment arrival counters (int32, zero between calls)]
-// [partial rows (float) D per head] [partial (m, l) pairs], 256-byte aligned.
-int64_t counter_bytes(int64_t segments) { return (segments * 4 + 255) / 256 * 256; }
+// [partial rows (float) D per head] [partial (m, l) pairs].  The counter
+// region is the first workspace_bytes/64 (rounded up to 256) bytes whatever
+// the call, so calls of different batch sizes can share one workspace: a
+// call's partial rows never land where any call's counters live.  Every
+// segment brings at least 264 bytes of partials (one head of D+2 >= 66
+// floats), so a workspace that holds a call's partials holds its counters.
+int64_t counter_region(int64_t workspace_bytes) { return (workspace_bytes / 64 + 255) / 256 * 256; }
 
 int64_t workspace_total(int64_t slots, int64_t segments, const Geometry& g, int D) {
-  return counter_bytes(segments) + workspace_floats(slots, g, D) * 4 + 256;
+  const int64_t pb = workspace_floats(slots, g, D) * 4;
+  int64_t w = (pb + pb / 63 + 1024 + 255) / 256 * 256;
+  while (w - counter_region(w) < pb || counter_region(w) < segments * 4) w += 256;
+  return w;
 }
 
 // Fill pipeline geometry, grid size and scratch pointers; launch both kernels.
@@ -193,13 +201,14 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
 
   const int64_t segments = (int64_t)geo.ngroups * p.num_seqs;
   const int64_t slots = nc + segments - 1;
-  const int64_t need = workspace_total(slots, segments, geo, D);
   if (!workspace) return SLMT_ERR_WORKSPACE;
-  if (workspace_bytes < need) return SLMT_ERR_WORKSPACE;
+  const int64_t creg = counter_region(workspace_bytes);
+  if (creg < segments * 4 || workspace_bytes - creg < workspace_floats(slots, geo, D) * 4)
+    return SLMT_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return SLMT_ERR_ALIGN;
   uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
   p.seg_count = reinterpret_cast<int32_t*>(w);
-  p.part_acc = reinterpret_cast<float*>(w + counter_bytes(segments));
+  p.part_acc = reinterpret_cast<float*>(w + creg);
   p.part_ml = p.part_acc + slots * (int64_t)geo.kvc * geo.G * D;
   p.out = out;
   p.out_dtype = out_dtype;

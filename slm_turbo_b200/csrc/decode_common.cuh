@@ -25,19 +25,6 @@ enum Layout : int {
   LAYOUT_PER_TOKEN = 2,    // [B, KV, S, D/2] codes + [B, KV, S] min/step
 };
 
-// ---- token order inside a staged 16-token tile ----
-// A consumer lane reads 8-byte words of fragment rows {g} (QK, rulers) and
-// {2r, 2r+1} (PV) of each tile; a wavefront serves 4 rows x 32 bytes, which
-// is conflict-free only if the 4 rows start on distinct 32-byte bank
-// groups.  Paged rows are staged back to back by whole-tile bulk copies (a
-// copy per row, which could pad rows apart, delivers the data much later),
-// so with a row stride of 64 mod 128 bytes (8 kv heads) only two groups
-// exist.  Reading fragment row i from token tok_of(i) -- the second pair of
-// every 4 swapped -- spreads the PV rows {0,2,4,6} over both groups (2-way
-// instead of 4-way), and makes both reads conflict-free at 32 or 96 mod 128
-// (4 kv heads at D = 64 or 128).
-__host__ __device__ constexpr int tok_of(int i) { return i ^ ((i >> 2) & 1); }
-
 // One descriptor per pipeline stage, written by the producer warp.
 struct ChunkDesc {
   int seq;        // sequence index, -1 = no more work

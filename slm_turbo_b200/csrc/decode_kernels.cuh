@@ -165,12 +165,6 @@ struct StageView {
   }
 };
 
-// Stage row (token) behind fragment row i of a consumer's tiles.
-template <int D, int LAYOUT, int KVC>
-__device__ __forceinline__ int stage_tok(int i) {
-  if constexpr (LAYOUT == LAYOUT_PAGED) return tok_of(i);
-  return i;
-}
 
 // ------------------------------------------------------------------ producer --
 // Page ids of 32 consecutive 16-token tiles of sequence s, one per lane.
@@ -680,14 +674,13 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   constexpr int VALIGN = (VB % 8 == 0) ? 8 : ((VB % 4 == 0) ? 4 : 1);
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, r = lane & 3;
-  // stage rows (tokens) behind this lane's fragment rows: QK / scores use
-  // rows g and g+8 of each tile, PV uses rows 2r, 2r+1, 2r+8, 2r+9
+  // QK / scores use token rows g and g+8 of each tile, PV rows 2r, 2r+1,
+  // 2r+8, 2r+9
   using SV = StageView<D, LAYOUT, KVC>;
-  const int gt = stage_tok<D, LAYOUT, KVC>(g);
-  const uint8_t* krow = sv.k(gt);  // + a*d16 + h*d8 -> row 16a + g + 8h
-  const uint8_t* rrow = sv.rulers(gt);
-  const uint8_t* vrow0 = sv.v(stage_tok<D, LAYOUT, KVC>(2 * r));
-  const uint8_t* vrow1 = sv.v(stage_tok<D, LAYOUT, KVC>(2 * r + 1));
+  const uint8_t* krow = sv.k(g);  // + a*d16 + h*d8 -> row 16a + g + 8h
+  const uint8_t* rrow = sv.rulers(g);
+  const uint8_t* vrow0 = sv.v(2 * r);
+  const uint8_t* vrow1 = sv.v(2 * r + 1);
 
   // ---- QK on biased codes, tile by tile (one accumulator chain per tile:
   // a second chain per tile costs registers the kernel does not have) ----
@@ -757,7 +750,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
 #pragma unroll
   for (int a = 0; a < 2; ++a)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * a + gt + 8 * h) < nvalid;
+    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * a + g + 8 * h) < nvalid;
 
   // ---- scores + online softmax (log2 domain, lazy rescale) ----
   const float sl2 = p.scale_log2;
@@ -846,8 +839,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   // ---- PV on biased codes: O^T[dims x heads] += (V^T + bias) . P'^T, one
   // k-step per tile; the same P' against a ones tile gives sum_t P'_t per
   // head, exactly as the tensor core sums it, to take the bias off later ----
-  // thread (g, r) needs fragment rows 16a + {2r, 2r+1, 2r+8, 2r+9} (tokens
-  // through tok_of), bytes [g*VB, +VB)
+  // thread (g, r) needs tokens 16a + {2r, 2r+1, 2r+8, 2r+9}, bytes [g*VB, +VB)
   constexpr uint32_t kOnes = 0x3C003C00u;  // fp16x2 (1, 1)
 #pragma unroll
   for (int a = 0; a < 2; ++a) {
@@ -881,6 +873,27 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
           for (int nt = 0; nt < NT; ++nt) mma_16816(w.acc[mt][nt], a0, a1, a2, a3, pb[a][nt][0], pb[a][nt][1]);
         }
       }
+    }
+  }
+}
+
+// Take the V-code bias out of the PV accumulator: rows g hold 1024 + c,
+// rows g+8 hold 64 + c, so acc -= bias * sum_t P'_t, and the sum restarts.
+// Done every few chunks, not only at the segment end: the tensor core's
+// fp32 accumulation errs by a fraction of the accumulator's magnitude, and
+// the bias would otherwise grow that magnitude over a long segment.
+template <int D, int NT>
+__device__ __forceinline__ void fold_v_bias(WarpState<D, NT>& w) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        w.acc[mt][nt][e] = fmaf(-1024.f, w.ps[nt][e], w.acc[mt][nt][e]);
+        w.acc[mt][nt][e + 2] = fmaf(-64.f, w.ps[nt][e], w.acc[mt][nt][e + 2]);
+      }
+      w.ps[nt][e] = 0.f;
     }
   }
 }
@@ -1008,6 +1021,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 
     if (flags & 2) {
       // ---- segment end: write the output, or a partial + maybe merge ----
+      fold_v_bias(w);
       const ChunkDesc& dd = hdr->desc[stage];  // still owned: released below
       const int ncov = dd.ncov, c_first = dd.c_first;
       const int e_seg = dd.kg * p.num_seqs + dd.seq;
@@ -1044,8 +1058,8 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
             float* dst = p.part_acc + row * D + 2 * g * VB;
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
-              float o0 = fmaf(-1024.f, w.ps[nt][e], w.acc[mt][nt][e]) + vsum;
-              float o1 = fmaf(-64.f, w.ps[nt][e], w.acc[mt][nt][e + 2]) + vsum;
+              float o0 = w.acc[mt][nt][e] + vsum;
+              float o1 = w.acc[mt][nt][e + 2] + vsum;
               if (LAYOUT == LAYOUT_PER_CHANNEL && p.use_quant) {
                 const int d0 = 2 * (g * VB + mt);
                 o0 = __half2float(vsc[d0]) * (o0 - __half2float(vze[d0]) * lsum);
@@ -1086,6 +1100,8 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       __syncwarp();
       if (lane == 0) mbar_arrive(&hdr->empty[stage]);
       ++seg;
+    } else if (stage == 0 && phase == 0) {
+      fold_v_bias(w);  // once per two turns of the stage ring
     }
 
     if (++stage == p.stages) {

@@ -72,11 +72,9 @@ extern "C" int slmt_paged_decode_noalloc(
   if (rc != SLMT_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (reset_scratch) {
-    // The counters occupy the first (kv groups x sequences) int32 words,
-    // rounded up to 256 bytes; num_kv_heads x num_seqs bounds the groups.
-    int64_t zero = (num_kv_heads * num_seqs * 4 + 255) / 256 * 256;
-    if (zero > (int64_t)SLMT_NOALLOC_SCRATCH_BYTES) zero = SLMT_NOALLOC_SCRATCH_BYTES;
-    if (zero > 0 && cudaMemsetAsync(scratch, 0, (size_t)zero, st) != cudaSuccess) return SLMT_ERR_CUDA;
+    // The counters occupy the first 1/64 of the array (rounded up to 256 bytes).
+    const size_t zero = ((size_t)SLMT_NOALLOC_SCRATCH_BYTES / 64 + 255) / 256 * 256;
+    if (cudaMemsetAsync(scratch, 0, zero, st) != cudaSuccess) return SLMT_ERR_CUDA;
   }
   return slmt_paged_decode(q, q_dtype, q_seq_stride, q_head_stride, kv_cache, num_blocks, block_size,
                            num_kv_heads, head_dim, block_tables, bt_dtype, bt_seq_stride,

@@ -189,3 +189,23 @@ def test_paged_decode_empty_runs_and_many_short_sequences():
                                          case["seq_lens"].to(dev))
         assert kd.read_device_errors(dev) == 0
         assert_close(got.cpu().numpy(), want, what=f"B={len(lengths)}")
+
+
+def test_workspace_shared_across_batch_shapes():
+    """One cached scratch serves calls of different shapes in any order: a
+    few long sequences with many heads (large partial rows) followed by many
+    short sequences (more segments, i.e. more arrival counters) must not read
+    the first call's partials as counters."""
+    kd = _kd()
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(41)
+    shapes = [([5000, 3000, 7000], 64, 8), (torch.randint(1, 90, (300,), generator=g).tolist(), 32, 8),
+              ([6000] * 2, 16, 2), (torch.randint(1, 400, (500,), generator=g).tolist(), 32, 8)]
+    for lengths, hq, kv in shapes:
+        case = ragged_paged_case(lengths, d=128, kv=kv, hq=hq, seed=len(lengths) + hq)
+        cache_cpu, cache_gpu = _store_both(case)
+        want = oracle.paged_decode(case["q"], cache_cpu, case["block_tables"], case["seq_lens"], 16, kv)
+        got = kd.kv_decode_paged_batched(case["q"].to(dev), cache_gpu, case["block_tables"].to(dev),
+                                         case["seq_lens"].to(dev))
+        assert kd.read_device_errors(dev) == 0
+        assert_close(got.cpu().numpy(), want, what=f"B={len(lengths)} hq={hq} kv={kv}")
