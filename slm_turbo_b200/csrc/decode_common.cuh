@@ -35,17 +35,23 @@ struct ChunkDesc {
   int slot;       // partial slot (cta + segment)
   int ncov;       // CTAs whose chunk ranges cover this segment
   int c_first;    // first of them
-  int pad[4];
+  int nmergers;   // how many of them end their range inside it (they merge it)
+  int pad[3];
 };
 
-// A segment whose partials this CTA merges after its main loop.
+// Descriptor flag bits.
+constexpr int kFlagFirst = 1;     // first chunk of the segment in this CTA
+constexpr int kFlagLast = 2;      // last chunk of the segment in this CTA
+constexpr int kFlagQbuf = 4;      // q buffer index (0/1)
+constexpr int kFlagRangeEnd = 8;  // last chunk of this CTA's range
+
+// The split segment this CTA helps merge after its main loop: the segment
+// its range ends in.  Every CTA whose range ends inside a split segment
+// merges a slice of its (head, dim-quad) items once all covering CTAs have
+// published their partials.
 struct MergeJob {
-  int e_seg, seq, kg, c_first, ncov;
+  int e_seg, seq, kg, c_first, ncov, nmergers;
 };
-
-// A CTA writes a partial (and may have to merge) only for a segment that
-// other CTAs also stream: at most its first and its last segment.
-constexpr int kMaxMerges = 4;
 
 struct SmemHeader {
   uint64_t full[kMaxStages];
@@ -53,9 +59,15 @@ struct SmemHeader {
   uint64_t qfull[2];
   uint64_t qempty[2];
   ChunkDesc desc[kMaxStages];
-  int nmerge;
-  MergeJob merges[kMaxMerges];
+  int has_job;
+  int merge_ok;
+  MergeJob job;
 };
+
+// Per-segment word in the scratch's counter region: low 16 bits count the
+// CTAs that published a partial, high 16 bits the mergers that are done;
+// the last merger resets the word to zero.
+constexpr uint32_t kArriveOne = 1u, kDoneOne = 1u << 16;
 
 constexpr int kHeaderBytes = (int)((sizeof(SmemHeader) + 127) / 128 * 128);
 

@@ -51,6 +51,27 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
   return v;
 }
 
+// Wait until the low 16 bits of `word` (published by other CTAs with a
+// fence before their atomic add) reach n; false after limit_ns.
+__device__ __forceinline__ bool spin_until_arrived(const unsigned int* word, unsigned int n,
+                                                   uint64_t limit_ns) {
+  auto arrived = [&]() {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(word) : "memory");
+    return (v & 0xFFFFu) >= n;
+  };
+  if (arrived()) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      __nanosleep(100);
+      if (arrived()) return true;
+    }
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
 __device__ __forceinline__ void set_err(const DecodeParams& p, uint32_t bit) {
   if (p.err) atomicOr(reinterpret_cast<unsigned int*>(p.err), bit);
 }
@@ -267,7 +288,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     int nch = nchunks_of(L);
     bool first = true;
     uint32_t seg = 0;  // segments started by this CTA
-    int seg_ncov = 1, seg_cfirst = c;
+    int seg_ncov = 1, seg_cfirst = c, seg_mergers = 0;
 
     // prefetched state: page-id windows of this segment (current, next) and
     // the next segment's length and first window
@@ -300,11 +321,16 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
         // CTAs whose ranges cover this segment (its chunk 0 is global chunk t - chunk)
         const long long p0 = t - chunk;
         seg_cfirst = (int)cta_of_unit(p0, T, nc_eff);
-        seg_ncov = (int)cta_of_unit(p0 + nch - 1, T, nc_eff) - seg_cfirst + 1;
+        const int c_last = (int)cta_of_unit(p0 + nch - 1, T, nc_eff);
+        seg_ncov = c_last - seg_cfirst + 1;
+        // CTAs c_first .. c_last-1 end their ranges inside the segment; c_last
+        // does too when the segment ends exactly where its range ends
+        seg_mergers = seg_ncov - 1 + (cta_start(c_last + 1, T, nc_eff) == p0 + nch ? 1 : 0);
       }
       const bool last = (chunk == nch - 1) || (t == t_end - 1);
       const int nvalid = min(kChunkTokens, L - chunk * kChunkTokens);
-      const int flags = (first ? 1 : 0) | (last ? 2 : 0) | (qb << 2);
+      const int flags = (first ? kFlagFirst : 0) | (last ? kFlagLast : 0) | (qb ? kFlagQbuf : 0) |
+                        (t == t_end - 1 ? kFlagRangeEnd : 0);
       const int slot = (int)(c + (int64_t)kg * B + s);
       uint8_t* dst = stg + (size_t)stage * p.stage_bytes;
       uint64_t* fb = &hdr->full[stage];
@@ -331,7 +357,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           const uint32_t tile_bytes = (uint32_t)(kTileTokens * row_bytes);
           const uint32_t tx = (ok0 ? tile_bytes : 0u) + (ok1 ? tile_bytes : 0u);
           if (lane == 0) {
-            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, {0, 0, 0, 0}};
+            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, {0, 0, 0}};
           }
           __syncwarp();
           if (lane == 0) {
@@ -358,7 +384,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           }
           const unsigned okm = __ballot_sync(0xffffffffu, ok);
           if (lane == 0) {
-            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, {0, 0, 0, 0}};
+            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, {0, 0, 0}};
           }
           const uint8_t* src =
               p.cache + ((phys * bs + (tok % bs)) * p.kv_total + (int64_t)kg * p.kvc) * SLOT;
@@ -396,7 +422,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           }
         }
         if (lane == 0) {
-          hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, {0, 0, 0, 0}};
+          hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, {0, 0, 0}};
         }
         const uint32_t tx = bulk ? (uint32_t)(2 * p.kvc * bytes) : 0u;
         __syncwarp();
@@ -550,7 +576,8 @@ __device__ __forceinline__ void consumer_bar() {
 // other CTAs' stores), then every thread folds the batch into the output
 // quads it owns, computing the log-sum-exp weights of their heads itself.
 template <int D, int KVC>
-__device__ void merge_segment(const DecodeParams& p, const MergeJob& job, float* scr, int scr_floats) {
+__device__ void merge_segment(const DecodeParams& p, const MergeJob& job, int i0, int i1, float* scr,
+                              int scr_floats) {
   constexpr int NTHR = KVC * 32;
   constexpr int Q = D / 4;
   constexpr int IPT = 4;  // output quads per thread per pass
@@ -565,8 +592,11 @@ __device__ void merge_segment(const DecodeParams& p, const MergeJob& job, float*
   const float2* ml2 = reinterpret_cast<const float2*>(p.part_ml);
   float* sRow = scr;                 // [nb][hp][D]
   float2* sMl = reinterpret_cast<float2*>(scr + nb * hp * D);  // [nb][hp]
-  for (int h0 = 0; h0 < hg; h0 += hp) {
-    const int hb = min(hp, hg - h0);
+  // items are (head, dim quad) pairs h*Q + q; this call owns [i0, i1)
+  const int hlo = i0 / Q, hhi = (i1 + Q - 1) / Q;
+  for (int h0 = hlo; h0 < hhi; h0 += hp) {
+    const int hb = min(hp, hhi - h0);
+    const int lo = max(i0 - h0 * Q, 0), hi = min(i1 - h0 * Q, hb * Q);  // local item range
     float4 a[IPT];
     float M[IPT], L[IPT];
 #pragma unroll
@@ -579,25 +609,25 @@ __device__ void merge_segment(const DecodeParams& p, const MergeJob& job, float*
       const int nbb = min(nb, np - p0);
       for (int i = 0; i < nbb; ++i) {
         const int64_t r = row0 + (int64_t)(p0 + i) * hg + h0;
-        for (int t = tid; t < hb * Q; t += NTHR) cp_async16_cg(sRow + (i * hp * D + 4 * t), acc4 + r * Q + t);
+        for (int t = lo + tid; t < hi; t += NTHR) cp_async16_cg(sRow + (i * hp * D + 4 * t), acc4 + r * Q + t);
       }
       // (m, l) pairs: two loads in flight per thread before either store, so
       // no thread serialises on one L2 round trip per partial.
       for (int t = tid; t < nbb * hb; t += 2 * NTHR) {
         const int t1 = t + NTHR;
-        const int i0 = t / hb, i1 = t1 / hb;
-        const float2 v0 = __ldcg(ml2 + row0 + (int64_t)(p0 + i0) * hg + h0 + (t - i0 * hb));
+        const int ia = t / hb, ib = t1 / hb;
+        const float2 v0 = __ldcg(ml2 + row0 + (int64_t)(p0 + ia) * hg + h0 + (t - ia * hb));
         float2 v1 = make_float2(0.f, 0.f);
-        if (t1 < nbb * hb) v1 = __ldcg(ml2 + row0 + (int64_t)(p0 + i1) * hg + h0 + (t1 - i1 * hb));
-        sMl[i0 * hp + (t - i0 * hb)] = v0;
-        if (t1 < nbb * hb) sMl[i1 * hp + (t1 - i1 * hb)] = v1;
+        if (t1 < nbb * hb) v1 = __ldcg(ml2 + row0 + (int64_t)(p0 + ib) * hg + h0 + (t1 - ib * hb));
+        sMl[ia * hp + (t - ia * hb)] = v0;
+        if (t1 < nbb * hb) sMl[ib * hp + (t1 - ib * hb)] = v1;
       }
       cp_async_wait_all();
       consumer_bar<KVC>();
 #pragma unroll
       for (int k = 0; k < IPT; ++k) {
-        const int item = k * NTHR + tid;
-        if (item < hb * Q) {
+        const int item = lo + k * NTHR + tid;
+        if (item < hi) {
           const int h = item / Q;
           float mx = M[k];
           for (int i = 0; i < nbb; ++i) mx = fmaxf(mx, sMl[i * hp + h].x);
@@ -625,8 +655,8 @@ __device__ void merge_segment(const DecodeParams& p, const MergeJob& job, float*
     }
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
-      const int item = k * NTHR + tid;
-      if (item < hb * Q) {
+      const int item = lo + k * NTHR + tid;
+      if (item < hi) {
         const int h = item / Q, q = item % Q;
         const float inv = (L[k] > 0.f) ? 1.f / L[k] : 0.f;
         const int64_t o = (int64_t)job.seq * p.out_seq_stride +
@@ -924,9 +954,9 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
     if (dsm.seq < 0) break;
     // fields needed after the stage is released are copied to registers
     const int flags = dsm.flags, slot = dsm.slot, nvalid = dsm.nvalid;
-    const int qbi = flags >> 2;
+    const int qbi = (flags & kFlagQbuf) ? 1 : 0;
 
-    if (flags & 1) {
+    if (flags & kFlagFirst) {
       // ---- segment start: q fragments, q sums, fresh softmax state ----
       if (!mbar_wait(&hdr->qfull[qbi], (seg / (uint32_t)p.nqbuf) & 1u, kWaitLimitNs)) {
         if (lane == 0) set_err(p, 4u);
@@ -1012,14 +1042,14 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       }
       // a segment's last chunk keeps its stage (and descriptor) until the
       // segment's output or partial is written
-      const bool rel = !(flags & 2);
+      const bool rel = !(flags & kFlagLast);
       if (nvalid == kChunkTokens)
         consume_chunk<D, NT, LAYOUT, KVC, false>(p, w, sv, nvalid, &hdr->empty[stage], rel);
       else
         consume_chunk<D, NT, LAYOUT, KVC, true>(p, w, sv, nvalid, &hdr->empty[stage], rel);
     }
 
-    if (flags & 2) {
+    if (flags & kFlagLast) {
       // ---- segment end: write the output, or a partial + maybe merge ----
       fold_v_bias(w);
       const ChunkDesc& dd = hdr->desc[stage];  // still owned: released below
@@ -1076,20 +1106,15 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
         }
       }
       if (!direct) {
-        // publish the partial; the last CTA to finish the segment merges it
-        // after its main loop (recorded in the shared merge list)
+        // publish the partial; if this CTA's range ends in the segment it
+        // merges a slice of it after its main loop
         __threadfence();
         consumer_bar<KVC>();
         if (threadIdx.x == 0) {
-          const int old = (ncov == 1) ? 0 : atomicAdd(reinterpret_cast<int*>(p.seg_count) + e_seg, 1);
-          if (old == ncov - 1) {
-            const int k = hdr->nmerge;
-            if (k < kMaxMerges) {
-              hdr->merges[k] = MergeJob{e_seg, seq, kgrp, c_first, ncov};
-              hdr->nmerge = k + 1;
-            } else {
-              set_err(p, 16u);  // cannot happen: bounded by the host (see kMaxMerges)
-            }
+          atomicAdd(reinterpret_cast<unsigned int*>(p.seg_count) + e_seg, kArriveOne);
+          if (flags & kFlagRangeEnd) {
+            hdr->job = MergeJob{e_seg, seq, kgrp, c_first, ncov, dd.nmergers};
+            hdr->has_job = 1;
           }
         }
       }
@@ -1110,16 +1135,34 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
     }
   }
 
-  // ---- merges of the segments this CTA finished last (the stage ring is
-  // idle now: every copy has landed and been consumed) ----
+  // ---- this CTA's slice of the merge of the split segment its range ends
+  // in (the stage ring is idle now: every copy has landed and been consumed) ----
   consumer_bar<KVC>();
-  const int nm = hdr->nmerge;
-  if (nm > 0) __threadfence();
-  for (int k = 0; k < nm; ++k) {
-    const MergeJob job = hdr->merges[k];
-    merge_segment<D, KVC>(p, job, reinterpret_cast<float*>(const_cast<uint8_t*>(stg)),
-                          p.stages * p.stage_bytes / 4);
-    if (threadIdx.x == 0 && job.ncov > 1) p.seg_count[job.e_seg] = 0;
+  if (hdr->has_job) {
+    const MergeJob job = hdr->job;
+    unsigned int* word = reinterpret_cast<unsigned int*>(p.seg_count) + job.e_seg;
+    if (threadIdx.x == 0) {
+      // every covering CTA publishes before it waits on anything, so this
+      // wait ends; it is bounded all the same
+      const bool ok = spin_until_arrived(word, (unsigned)job.ncov, kWaitLimitNs);
+      if (!ok) set_err(p, 4u);
+      hdr->merge_ok = ok ? 1 : 0;
+    }
+    consumer_bar<KVC>();
+    __threadfence();
+    if (hdr->merge_ok) {
+      const int items = kvc * G * (D / 4);
+      const int k = (int)blockIdx.x - job.c_first;
+      const int i0 = (int)((int64_t)k * items / job.nmergers);
+      const int i1 = (int)((int64_t)(k + 1) * items / job.nmergers);
+      merge_segment<D, KVC>(p, job, i0, i1, reinterpret_cast<float*>(const_cast<uint8_t*>(stg)),
+                            p.stages * p.stage_bytes / 4);
+      consumer_bar<KVC>();
+      if (threadIdx.x == 0) {
+        const unsigned int old = atomicAdd(word, kDoneOne);
+        if ((old >> 16) == (unsigned)job.nmergers - 1u) atomicExch(word, 0u);  // last merger: reset
+      }
+    }
   }
 }
 
@@ -1145,7 +1188,7 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
       mbar_init(&hdr->qfull[i], 1);
       mbar_init(&hdr->qempty[i], KVC);
     }
-    hdr->nmerge = 0;
+    hdr->has_job = 0;
     fence_mbar_init();
   }
   __syncthreads();
