@@ -20,38 +20,45 @@ using DecodeFn = void (*)(const DecodeParams);
 // The paged layout is instantiated per kv heads per stage row (KVC), so the
 // consumers' row addresses are compile-time offsets; the contiguous layouts
 // address rows with a per-warp base and need no such specialisation.
-template <int D, int NT, int KVC>
+template <int D, int NT, int KVC, bool PK>
 DecodeFn decode_fn_kvc(int layout) {
   switch (layout) {
     case LAYOUT_PAGED:
-      return decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC>;
+      return decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK>;
     case LAYOUT_PER_CHANNEL:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL, KVC>;
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL, KVC, PK>;
     default:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN, KVC>;
+      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN, KVC, PK>;
   }
 }
 
-// Instantiated per head dim, n-tiles and kv heads per CTA (compile-time
-// row strides, one consumer warp per kv head).
-template <int D, int NT>
+// Instantiated per head dim, n-tiles, kv heads per CTA (compile-time row
+// strides, one consumer warp per kv head) and tile packing (PK: at most 4
+// query heads per kv head, so two tiles share one n-tile).
+template <int D, int NT, bool PK>
 DecodeFn decode_fn_layout(int layout, int kvc) {
   switch (kvc) {
     case 8:
-      return decode_fn_kvc<D, NT, 8>(layout);
+      return decode_fn_kvc<D, NT, 8, PK>(layout);
     case 4:
-      return decode_fn_kvc<D, NT, 4>(layout);
+      return decode_fn_kvc<D, NT, 4, PK>(layout);
     case 2:
-      return decode_fn_kvc<D, NT, 2>(layout);
+      return decode_fn_kvc<D, NT, 2, PK>(layout);
     default:
-      return decode_fn_kvc<D, NT, 1>(layout);
+      return decode_fn_kvc<D, NT, 1, PK>(layout);
   }
 }
 
-DecodeFn decode_fn(int D, int nt, int layout, int kvc) {
-  if (D == 64) return nt == 1 ? decode_fn_layout<64, 1>(layout, kvc) : decode_fn_layout<64, 2>(layout, kvc);
-  if (D == 80) return nt == 1 ? decode_fn_layout<80, 1>(layout, kvc) : decode_fn_layout<80, 2>(layout, kvc);
-  return nt == 1 ? decode_fn_layout<128, 1>(layout, kvc) : decode_fn_layout<128, 2>(layout, kvc);
+template <int D>
+DecodeFn decode_fn_d(int nt, bool pk, int layout, int kvc) {
+  if (nt == 2) return decode_fn_layout<D, 2, false>(layout, kvc);
+  return pk ? decode_fn_layout<D, 1, true>(layout, kvc) : decode_fn_layout<D, 1, false>(layout, kvc);
+}
+
+DecodeFn decode_fn(int D, int nt, bool pk, int layout, int kvc) {
+  if (D == 64) return decode_fn_d<64>(nt, pk, layout, kvc);
+  if (D == 80) return decode_fn_d<80>(nt, pk, layout, kvc);
+  return decode_fn_d<128>(nt, pk, layout, kvc);
 }
 
 struct OccEntry {
@@ -106,6 +113,7 @@ namespace {
 
 struct Geometry {
   int G, nt, kvc, ngroups;
+  bool pk;  // two tiles share one n-tile (G <= 4)
 };
 
 int geometry(int64_t hq, int64_t kv, Geometry* g) {
@@ -121,6 +129,7 @@ int geometry(int64_t hq, int64_t kv, Geometry* g) {
   }
   g->G = (int)G;
   g->nt = G <= 8 ? 1 : 2;
+  g->pk = G <= 4;
   g->kvc = kvc;
   g->ngroups = (int)(kv / kvc);
   return SLMT_OK;
@@ -190,7 +199,7 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.nqbuf = nqbuf;
   p.stage_offset = stage_offset;
 
-  DecodeFn fn = decode_fn(D, geo.nt, layout, geo.kvc);
+  DecodeFn fn = decode_fn(D, geo.nt, geo.pk, layout, geo.kvc);
   const int occ = occupancy(dev, reinterpret_cast<const void*>(fn), threads, smem);
   if (occ <= 0) return SLMT_ERR_CUDA;
   const int64_t per_sm = std::min(occ, ctas_per_sm(geo.kvc, geo.nt));  // keeps the workspace bound

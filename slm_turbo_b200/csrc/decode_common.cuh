@@ -18,6 +18,7 @@ constexpr int kChunkTokens = 32;  // one pipeline stage = two tiles
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 0.2 s per drain wait
 constexpr float kRescaleSlack = 4.0f;  // lazy softmax rescale threshold (log2 units)
+constexpr float kMaxFloor = -1e30f;    // running max before any score (finite on purpose)
 
 enum Layout : int {
   LAYOUT_PAGED = 0,        // [num_blocks, block_size, KV, D+8] per-token slots

@@ -691,7 +691,13 @@ struct WarpState {
   float m[NT][2], l[NT][2], vs[NT][2];
 };
 
-template <int D, int NT, int LAYOUT, int KVC, bool MASK>
+// PK (one n-tile, at most 4 query heads per kv head): lanes of columns 4..7
+// carry the same query heads as columns 0..3, so one score fragment holds
+// tile 0's scores in columns 0..3 and tile 1's in columns 4..7 and the
+// softmax runs on useful columns only; PV feeds each tile its own columns.
+// The two column halves are two online-softmax streams over the even and
+// odd tiles, combined at the segment end.
+template <int D, int NT, int LAYOUT, int KVC, bool MASK, bool PK>
 __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D, NT>& w,
                                               const StageView<D, LAYOUT, KVC>& sv, int nvalid,
                                               uint64_t* empty_bar, bool release) {
@@ -711,6 +717,9 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   const uint8_t* rrow = sv.rulers(g);
   const uint8_t* vrow0 = sv.v(2 * r);
   const uint8_t* vrow1 = sv.v(2 * r + 1);
+  static_assert(!PK || NT == 1, "tile packing needs one n-tile");
+  constexpr int NA = PK ? 1 : 2;     // score tiles held per thread
+  const int at = PK ? (r >> 1) : 0;  // PK: the tile of this thread's columns
 
   // ---- QK on biased codes, tile by tile (one accumulator chain per tile:
   // a second chain per tile costs registers the kernel does not have) ----
@@ -765,6 +774,10 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
 #pragma unroll
       for (int i = 0; i < 4; ++i) sacc[a][nt][i] = c[nt][i];
   }
+  if constexpr (PK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sacc[0][0][i] = at ? sacc[1][0][i] : sacc[0][0][i];
+  }
 
   // ---- per-token rulers (k_min, k_step | v_min, v_step) are read from shared
   // memory where they are used, to keep registers free ----
@@ -776,23 +789,24 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(0.f, 1.f);
     return __half22float2(*reinterpret_cast<const __half2*>(rrow + a * SV::r16 + h * SV::r8 + 4));
   };
-  bool val[2][2];
+  auto tile = [&](int a) { return PK ? at : a; };
+  bool val[NA][2];
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
+  for (int a = 0; a < NA; ++a)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * a + g + 8 * h) < nvalid;
+    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * tile(a) + g + 8 * h) < nvalid;
 
   // ---- scores + online softmax (log2 domain, lazy rescale) ----
   const float sl2 = p.scale_log2;
-  float sc[2][NT][4];
+  float sc[NA][NT][4];
   float mx[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) mx[nt][0] = mx[nt][1] = -INFINITY;
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
+  for (int a = 0; a < NA; ++a) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float2 kr = ruler_k(a, h);
+      const float2 kr = ruler_k(tile(a), h);
       const float kst = kr.y * sl2;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -841,16 +855,16 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     }
   }
 
-  uint32_t pb[2][NT][2];
+  uint32_t pb[NA][NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NA; ++a) {
       float pp[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int h = i >> 1, e = i & 1;
-        const float2 vr = ruler_v(a, h);
+        const float2 vr = ruler_v(tile(a), h);
         const float pe = exp2_approx(sc[a][nt][i] - w.m[nt][e]);  // 0 for masked rows
         w.l[nt][e] += pe;
         if (MASK) {
@@ -872,10 +886,25 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   // thread (g, r) needs tokens 16a + {2r, 2r+1, 2r+8, 2r+9}, bytes [g*VB, +VB)
   constexpr uint32_t kOnes = 0x3C003C00u;  // fp16x2 (1, 1)
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
+  for (int a = 0; a < NA; ++a)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
       mma_16816_rows0(w.ps[nt][0], w.ps[nt][1], kOnes, kOnes, kOnes, kOnes, pb[a][nt][0], pb[a][nt][1]);
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
+    // B operand of tile a: PK keeps only the columns of tile a (B column = g)
+    uint32_t pbt[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if constexpr (PK) {
+        const bool mine = (g >= 4) == (a == 1);
+        pbt[nt][0] = mine ? pb[0][nt][0] : 0u;
+        pbt[nt][1] = mine ? pb[0][nt][1] : 0u;
+      } else {
+        pbt[nt][0] = pb[a][nt][0];
+        pbt[nt][1] = pb[a][nt][1];
+      }
+    }
     uint32_t vw[4][VW];
     load_bytes<VB, VALIGN>(vrow0 + a * SV::d16 + g * VB, vw[0]);
     load_bytes<VB, VALIGN>(vrow1 + a * SV::d16 + g * VB, vw[1]);
@@ -900,7 +929,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
           const uint32_t a0 = codes_lo_biased(w1), a1 = codes_hi_biased(w1);
           const uint32_t a2 = codes_lo_biased(w2), a3 = codes_hi_biased(w2);
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_16816(w.acc[mt][nt], a0, a1, a2, a3, pb[a][nt][0], pb[a][nt][1]);
+          for (int nt = 0; nt < NT; ++nt) mma_16816(w.acc[mt][nt], a0, a1, a2, a3, pbt[nt][0], pbt[nt][1]);
         }
       }
     }
@@ -928,7 +957,7 @@ __device__ __forceinline__ void fold_v_bias(WarpState<D, NT>& w) {
   }
 }
 
-template <int D, int NT, int LAYOUT, int KVC>
+template <int D, int NT, int LAYOUT, int KVC, bool PK>
 __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
                                 const uint8_t* qbuf, const uint8_t* rbuf,
                                 const uint8_t* stg) {
@@ -972,7 +1001,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       for (int s = 0; s < KS; ++s) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const int n = nt * 8 + g;
+          const int n = PK ? (g & 3) : nt * 8 + g;  // PK: columns 4..7 repeat heads 0..3
           float x[4] = {0.f, 0.f, 0.f, 0.f};
           if (n < G) {
 #pragma unroll
@@ -1013,7 +1042,9 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
         w.qs[nt][1] = __shfl_sync(0xffffffffu, v, (2 * r + 1) * 4) * p.scale_log2;
         w.qb[nt][0] = __shfl_sync(0xffffffffu, bv, (2 * r) * 4);
         w.qb[nt][1] = __shfl_sync(0xffffffffu, bv, (2 * r + 1) * 4);
-        w.m[nt][0] = w.m[nt][1] = -INFINITY;
+        // a finite floor (not -inf): a stream whose tokens in a chunk are all
+        // masked must give exp2(-inf - m) = 0, not NaN
+        w.m[nt][0] = w.m[nt][1] = kMaxFloor;
         w.l[nt][0] = w.l[nt][1] = 0.f;
         w.vs[nt][0] = w.vs[nt][1] = 0.f;
 #pragma unroll
@@ -1044,9 +1075,9 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       // segment's output or partial is written
       const bool rel = !(flags & kFlagLast);
       if (nvalid == kChunkTokens)
-        consume_chunk<D, NT, LAYOUT, KVC, false>(p, w, sv, nvalid, &hdr->empty[stage], rel);
+        consume_chunk<D, NT, LAYOUT, KVC, false, PK>(p, w, sv, nvalid, &hdr->empty[stage], rel);
       else
-        consume_chunk<D, NT, LAYOUT, KVC, true>(p, w, sv, nvalid, &hdr->empty[stage], rel);
+        consume_chunk<D, NT, LAYOUT, KVC, true, PK>(p, w, sv, nvalid, &hdr->empty[stage], rel);
     }
 
     if (flags & kFlagLast) {
@@ -1070,6 +1101,26 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
           l1 += __shfl_xor_sync(0xffffffffu, l1, o);
           u0 += __shfl_xor_sync(0xffffffffu, u0, o);
           u1 += __shfl_xor_sync(0xffffffffu, u1, o);
+        }
+        if constexpr (PK) {
+          // lane r^2 holds the other tile parity's stream of the same heads
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float mo = __shfl_xor_sync(0xffffffffu, w.m[nt][e], 2);
+            const float mn = fmaxf(w.m[nt][e], mo);
+            const float s0 = exp2_approx(w.m[nt][e] - mn), s1 = exp2_approx(mo - mn);
+            float& lr = e ? l1 : l0;
+            float& ur = e ? u1 : u0;
+            lr = lr * s0 + __shfl_xor_sync(0xffffffffu, lr, 2) * s1;
+            ur = ur * s0 + __shfl_xor_sync(0xffffffffu, ur, 2) * s1;
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+              w.acc[mt][nt][e] = w.acc[mt][nt][e] * s0 + __shfl_xor_sync(0xffffffffu, w.acc[mt][nt][e], 2) * s1;
+              w.acc[mt][nt][e + 2] =
+                  w.acc[mt][nt][e + 2] * s0 + __shfl_xor_sync(0xffffffffu, w.acc[mt][nt][e + 2], 2) * s1;
+            }
+            w.m[nt][e] = mn;
+          }
         }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
@@ -1171,7 +1222,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 // CTAs per SM are chosen for about 18 warps per SM with one n-tile (96
 // registers: a sub-partition holds up to 5 warps of its 16K registers) and
 // about 9 with two n-tiles.
-template <int D, int NT, int LAYOUT, int KVC>
+template <int D, int NT, int LAYOUT, int KVC, bool PK>
 __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
     decode_splitk_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1195,7 +1246,7 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
   if (threadIdx.x >= KVC * 32)
     decode_producer<D, LAYOUT>(p, hdr, qbuf, rbuf, stg);
   else
-    decode_consumer<D, NT, LAYOUT, KVC>(p, hdr, qbuf, rbuf, stg);
+    decode_consumer<D, NT, LAYOUT, KVC, PK>(p, hdr, qbuf, rbuf, stg);
 }
 
 }  // namespace slmt
