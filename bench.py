@@ -515,6 +515,161 @@ def run_ours(args):
     return 0
 
 
+# ----------------------------------------------------- extra workload lines
+def _dist_setup():
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    return world, rank, dev, pg
+
+
+def _timed(dev, pg, fn, steps, warmup, n_sets=1):
+    """Warm-up, then `steps` calls of fn(i) between CUDA events on the current
+    stream, barrier + synchronize on both sides; max over ranks (ms/step)."""
+    for i in range(max(warmup, 3)):
+        fn(i % n_sets)
+    torch.cuda.synchronize(dev)
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for i in range(steps):
+            fn(i % n_sets)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    if pg is not None:
+        pg.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    if pg is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, clk.summary()
+
+
+def run_c2(args):
+    """uniform batched decode over the standalone
+    per-channel layout, B=16 x 2048 tokens, Hq32/Hkv8, D = --head-dim.  The
+    working set of one step (34 MB at D=128) fits in L2, so the timed steps
+    rotate over 4 independent input sets (136 MB) and every step reads cold
+    data.  One step = one batched decode launch; sequences are split over
+    ranks (weak scaling)."""
+    world, rank, dev, pg = _dist_setup()
+    from slm_turbo_b200.kernels import kv_dequant as kd
+    B, Hq, KV, S, Dh, NSETS = 16, 32, 8, 2048, args.head_dim, 4
+    g = torch.Generator(device=dev).manual_seed(SEED + 20 + rank)
+    sets = []
+    for _ in range(NSETS):
+        k = torch.randn(B, KV, S, Dh, device=dev, generator=g).half()
+        v = torch.randn(B, KV, S, Dh, device=dev, generator=g).half()
+        kp, ks, kz = kd.kv_quantize_per_channel(k)
+        vp, vs, vz = kd.kv_quantize_per_channel(v)
+        q = torch.randn(B, Hq, Dh, device=dev, generator=g).half()
+        sets.append((q, kp, ks, kz, vp, vs, vz, torch.empty(B, Hq, Dh, dtype=torch.float32, device=dev)))
+        del k, v
+    torch.cuda.synchronize(dev)
+
+    def step(i):
+        q, kp, ks, kz, vp, vs, vz, out = sets[i]
+        kd.kv_dequant_decode_attention_batched(q, kp, ks, kz, vp, vs, vz, out=out)
+
+    ms, clocks = _timed(dev, pg, step, args.steps, args.warmup, NSETS)
+    assert kd.read_device_errors(dev) == 0
+    byts = B * KV * S * (Dh // 2) * 2 + B * KV * Dh * 2 * 4 + B * Hq * Dh * (2 + 4)
+    peak, peak_src = measured_peak()
+    achieved = byts / (ms * 1e-3) / 1e9
+    if pg is not None:
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    print(json.dumps({
+        "metric": METRIC, "value": B * world / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"C2 per-channel batched decode: per GPU 16 seqs x 2048, Hq32/Hkv8/D{Dh}",
+                   "l2": f"{NSETS} rotating input sets ({NSETS * byts / 1e6:.0f} MB > L2)",
+                   "parallelism": f"seq-partition x{world} (no collective)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": f"decode_splitk_kernel<{Dh},1,PER_CHANNEL,8,1>",
+                     "algorithmic_bytes_per_launch": byts, "peak_source": peak_src},
+        "e2e": None, "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": None}), flush=True)
+    return 0
+
+
+def run_c4(args):
+    """long-context decode, 4 sequences of 131,072 tokens,
+    Hq64/Hkv8/D128, paged per-token 4-bit, block 16; split-K over the
+    sequence inside a GPU, kv heads sharded over ranks (strong scaling: each
+    rank holds 8/N kv heads and their 64/N query heads).  One step = append
+    one token per sequence + decode."""
+    world, rank, dev, pg = _dist_setup()
+    from slm_turbo_b200.kernels import kv_dequant as kd
+    from slm_turbo_b200.sharding import shard_kv_heads
+    B, L, Hq_all, KV_all = 4, 131072, 64, 8
+    heads = shard_kv_heads(KV_all, world, rank)
+    kv = len(heads)
+    hq = Hq_all // KV_all * kv
+    nblk = (L + 1 + BS - 1) // BS
+    gen = torch.Generator().manual_seed(SEED + 40)
+    perm = torch.randperm(B * nblk, generator=gen)
+    bt = perm.view(B, nblk).to(torch.int32).to(dev)
+    cache = torch.empty(B * nblk, BS, kv, D + 8, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(SEED + 41 + rank)
+    chunk = 16384
+    for b in range(B):
+        for t0 in range(0, L, chunk):
+            t = torch.arange(t0, min(L, t0 + chunk), device=dev)
+            slots = bt[b, t // BS].to(torch.int64) * BS + t % BS
+            k = torch.randn(len(t), kv, D, device=dev, generator=g).half()
+            v = torch.randn(len(t), kv, D, device=dev, generator=g).half()
+            kd.kv_quantize_store(k, v, cache, slots, BS)
+    sl = torch.full((B,), L + 1, dtype=torch.int32, device=dev)
+    pos = torch.full((B,), L, dtype=torch.int64, device=dev)
+    slots_new = bt[torch.arange(B, device=dev), pos // BS].to(torch.int64) * BS + pos % BS
+    q = torch.randn(B, hq, D, device=dev, generator=g).half()
+    k_new = torch.randn(B, kv, D, device=dev, generator=g).half()
+    v_new = torch.randn(B, kv, D, device=dev, generator=g).half()
+    out = torch.empty(B, hq, D, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+
+    def step(_):
+        kd.kv_quantize_store(k_new, v_new, cache, slots_new, BS)
+        kd.kv_decode_paged_batched(q, cache, bt, sl, out=out, max_seq_len=L + 1)
+
+    ms, clocks = _timed(dev, pg, step, args.steps, args.warmup)
+    assert kd.read_device_errors(dev) == 0
+    byts = B * (L + 1) * kv * (D + 8) + B * nblk * 4 + B * hq * D * (2 + 4)
+    peak, peak_src = measured_peak()
+    achieved = byts / (ms * 1e-3) / 1e9
+    if pg is not None:
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    print(json.dumps({
+        "metric": METRIC, "value": B / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "C4 long-context paged 4-bit decode: 4 seqs x 131072 (+1 appended token/step), "
+                               "Hq64/Hkv8/D128, block 16",
+                   "kv_heads_per_gpu": kv, "pool_mb_per_gpu": round(B * nblk * BS * kv * (D + 8) / 1e6, 1),
+                   "l2": "inputs larger than L2, no flush",
+                   "parallelism": f"kv-head shards x{world} (no collective)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "kv_store_kernel + decode_splitk_kernel (step, rank 0)",
+                     "algorithmic_bytes_per_launch": byts, "peak_source": peak_src},
+        "e2e": None, "gpu_launches": 2 * args.steps, "clocks": clocks, "cpu_baseline": None}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -523,9 +678,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", default="c3", choices=["c3", "c2", "c4"],
+                    help="c3 (default, the metric's config); c2 / c4 print extra lines")
+    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128], help="c2 only")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "c2":
+        return run_c2(args)
+    if args.workload == "c4":
+        return run_c4(args)
     return run_ours(args)
 
 

@@ -8,7 +8,7 @@ namespace slmt {
 
 namespace {
 
-constexpr int kMinChunksPerCta = 2;    // do not split below ~64 tokens per CTA
+constexpr int kMinChunksPerCta = 4;    // do not split below ~128 tokens per CTA
 constexpr int kSmemPerSm = 233472;     // 228 KB shared memory per SM (sm_100)
 constexpr int kSmemPerCtaMax = 232448; // 227 KB opt-in per CTA
 constexpr int kSmemReserved = 1024;    // reserved per resident CTA
@@ -298,6 +298,11 @@ int contig_decode(int layout, const void* q, int q_dtype, int64_t q_seq_stride,
   p.use_quant = use_quant ? 1 : 0;
   p.contig_bulk_ok = (ka % 16 == 0) && (va % 16 == 0) && ((s_cap * half) % 16 == 0) &&
                      ((kv_seq_stride_rows * half) % 16 == 0);
+  // rulers [B, KV, D] fp16: a kv group's rows are one span of kvc*D values
+  const bool rul_al = ((reinterpret_cast<uintptr_t>(r0) | reinterpret_cast<uintptr_t>(r1) |
+                        reinterpret_cast<uintptr_t>(r2) | reinterpret_cast<uintptr_t>(r3)) % 16 == 0);
+  p.rul_bulk = (layout == LAYOUT_PER_CHANNEL) && use_quant && rul_al && ((ruler_seq_stride * 2) % 16 == 0) &&
+               ((geo.kvc * D * 2) % 16 == 0);
   p.seq_lens = seq_lens;
   p.seq_len_scalar = (int)seq_len_scalar;
   p.causal_rows = causal_rows ? 1 : 0;

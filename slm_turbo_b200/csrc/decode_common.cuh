@@ -96,6 +96,7 @@ struct DecodeParams {
   const uint16_t* r3;  // per-channel v_zero  | per-token v_step
   int64_t ruler_seq_stride;
   int use_quant, contig_bulk_ok;
+  int rul_bulk;  // per-channel rulers of a kv group: four 16-byte aligned spans
   // lengths
   const int32_t* seq_lens;
   int seq_len_scalar, causal_rows, len_cap;

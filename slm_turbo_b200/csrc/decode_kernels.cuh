@@ -470,26 +470,32 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
         else
           for (int i = lane; i < hg * D; i += 32)
             reinterpret_cast<uint16_t*>(qd)[i] = qsrc[(int64_t)(i / D) * p.q_head_stride + i % D];
-        if (LAYOUT == LAYOUT_PER_CHANNEL) {
-          uint16_t* rd = reinterpret_cast<uint16_t*>(rbuf + qb * p.rbuf_bytes);
-          for (int i = lane; i < 4 * p.kvc * D; i += 32) {
-            const int a = i / (p.kvc * D), rem = i % (p.kvc * D);
-            const int jj = rem / D, d = rem % D;
-            const int kvh = kg * p.kvc + jj;
-            uint16_t v;
-            if (p.use_quant) {
-              const uint16_t* src = (a == 0) ? p.r0 : (a == 1) ? p.r1 : (a == 2) ? p.r2 : p.r3;
-              v = src[(int64_t)s * p.ruler_seq_stride + (int64_t)kvh * D + d];
-            } else {
-              v = (a & 1) ? (uint16_t)0 : (uint16_t)0x3C00u;  // scale 1, zero 0
+        // per-channel rulers (only read when use_quant): the group's kvc*D
+        // values of k_scale, k_zero, v_scale, v_zero, one contiguous span each
+        uint16_t* rd = reinterpret_cast<uint16_t*>(rbuf + qb * p.rbuf_bytes);
+        const int64_t rsrc = (int64_t)s * p.ruler_seq_stride + (int64_t)kg * p.kvc * D;
+        const int span = p.kvc * D;
+        uint32_t rtx = 0;
+        if (LAYOUT == LAYOUT_PER_CHANNEL && p.use_quant) {
+          if (p.rul_bulk) {
+            rtx = (uint32_t)(4 * span * 2);
+          } else {
+            for (int a = 0; a < 4; ++a) {
+              const uint16_t* src = ((a == 0) ? p.r0 : (a == 1) ? p.r1 : (a == 2) ? p.r2 : p.r3) + rsrc;
+              for (int i = lane; i < span; i += 32) rd[a * span + i] = src[i];
             }
-            rd[i] = v;
           }
         }
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive_expect_tx(&hdr->qfull[qb], qtx);
+          mbar_arrive_expect_tx(&hdr->qfull[qb], qtx + rtx);
           if (qtx) bulk_g2s(qd, qsrc, qtx, &hdr->qfull[qb], policy);
+          if (rtx) {
+            bulk_g2s(rd, p.r0 + rsrc, (uint32_t)(span * 2), &hdr->qfull[qb], policy);
+            bulk_g2s(rd + span, p.r1 + rsrc, (uint32_t)(span * 2), &hdr->qfull[qb], policy);
+            bulk_g2s(rd + 2 * span, p.r2 + rsrc, (uint32_t)(span * 2), &hdr->qfull[qb], policy);
+            bulk_g2s(rd + 3 * span, p.r3 + rsrc, (uint32_t)(span * 2), &hdr->qfull[qb], policy);
+          }
         }
       }
 

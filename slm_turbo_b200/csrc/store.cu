@@ -9,6 +9,8 @@
 //    kernels/benchmark/benchmark.py:26-56 on the device, with the same
 //    fp16 arithmetic (each op computed in fp32 and rounded to fp16, as torch
 //    evaluates half tensors).
+#include <cooperative_groups.h>
+
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -185,6 +187,153 @@ __global__ void __launch_bounds__(256) pc_codes_kernel(
   }
 }
 
+// Vector path of the per-channel quantizer: rows of D fp16 values that start
+// on 16 bytes (D = 64, 80, 128 are multiples of 8 values).
+constexpr int kPcSplit = 8;  // CTAs (one cluster) per row of the rulers pass
+
+// Rulers, one cluster of kPcSplit CTAs per (seq*kv) row: CTA k reduces tokens
+// [k*S/split, (k+1)*S/split) with 16-byte loads (8 dims per thread), the
+// cluster's rank 0 combines the 8 partial min/max sets through distributed
+// shared memory and writes scale/zero exactly as pc_rulers_kernel does.
+template <int D>
+__global__ void __cluster_dims__(kPcSplit, 1, 1) __launch_bounds__(256)
+    pc_rulers_vec_kernel(const __half* __restrict__ x, int64_t S, uint16_t* __restrict__ scale,
+                         uint16_t* __restrict__ zero) {
+  namespace cg = cooperative_groups;
+  constexpr int LPR = D / 8;           // threads per token row
+  constexpr int RPI = 256 / LPR;       // token rows per iteration
+  __shared__ float smn[RPI][D], smx[RPI][D];
+  __shared__ float cmn[D], cmx[D];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int row = blockIdx.x / kPcSplit;
+  const int part = (int)cluster.block_rank();
+  const int tid = threadIdx.x;
+  const int rs = tid / LPR, dg = tid % LPR;  // token-row slot, 8-dim group
+  const int64_t s0 = part * S / kPcSplit, s1 = (part + 1) * S / kPcSplit;
+  float mn[8], mx[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    mn[i] = INFINITY;
+    mx[i] = -INFINITY;
+  }
+  if (rs < RPI) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + ((int64_t)row * S) * D) + dg;
+#pragma unroll 4
+    for (int64_t t = s0 + rs; t < s1; t += RPI) {
+      const uint4 u = __ldg(xr + t * (D / 8));
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        mn[2 * i] = fminf(mn[2 * i], f.x);
+        mx[2 * i] = fmaxf(mx[2 * i], f.x);
+        mn[2 * i + 1] = fminf(mn[2 * i + 1], f.y);
+        mx[2 * i + 1] = fmaxf(mx[2 * i + 1], f.y);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      smn[rs][dg * 8 + i] = mn[i];
+      smx[rs][dg * 8 + i] = mx[i];
+    }
+  }
+  __syncthreads();
+  for (int d = tid; d < D; d += 256) {
+    float a = INFINITY, b = -INFINITY;
+    for (int k = 0; k < RPI; ++k) {
+      a = fminf(a, smn[k][d]);
+      b = fmaxf(b, smx[k][d]);
+    }
+    cmn[d] = a;
+    cmx[d] = b;
+  }
+  cluster.sync();
+  if (part == 0) {
+    for (int d = tid; d < D; d += 256) {
+      float a = cmn[d], b = cmx[d];
+      for (int k = 1; k < kPcSplit; ++k) {
+        a = fminf(a, cluster.map_shared_rank(cmn, k)[d]);
+        b = fmaxf(b, cluster.map_shared_rank(cmx, k)[d]);
+      }
+      float sc = h16(__fdiv_rn(h16(__fsub_rn(b, a)), 15.0f));
+      float zp = h16(__fsub_rn(0.0f, rintf(h16(__fdiv_rn(a, sc)))));
+      if (b == a) {
+        sc = 1.0f;
+        zp = 0.0f;
+      }
+      zp = fminf(fmaxf(zp, 0.0f), 15.0f);
+      const int64_t o = (int64_t)row * D + d;
+      scale[o] = __half_as_ushort(__float2half_rn(sc));
+      zero[o] = __half_as_ushort(__float2half_rn(zp));
+    }
+  }
+  cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
+}
+
+// Codes, 16 dims per thread: two 16-byte loads of x, the rulers of those
+// dims, one 8-byte store of packed codes.  Item i = (h, t, g) with g the
+// 16-dim group; x rows and rulers as pc_codes_kernel.
+template <int D>
+__global__ void __launch_bounds__(256) pc_codes_vec_kernel(
+    const __half* __restrict__ x, int64_t xh, int64_t xt, int64_t heads, int64_t ntok,
+    const uint16_t* __restrict__ scale, const uint16_t* __restrict__ zero, int64_t ruler_h,
+    uint8_t* __restrict__ packed, int64_t s_cap, int64_t pos) {
+  constexpr int G = D / 16;
+  const int64_t total = heads * ntok * G;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(i % G);
+    const int64_t ht = i / G;
+    const int64_t t = ht % ntok, h = ht / ntok;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + h * xh + t * xt + 16 * g);
+    const uint4 u0 = __ldg(xr), u1 = __ldg(xr + 1);
+    const uint4* sr = reinterpret_cast<const uint4*>(scale + h * ruler_h + 16 * g);
+    const uint4* zr = reinterpret_cast<const uint4*>(zero + h * ruler_h + 16 * g);
+    const uint4 s0 = __ldg(sr), s1 = __ldg(sr + 1), z0 = __ldg(zr), z1 = __ldg(zr + 1);
+    const __half* xv0 = reinterpret_cast<const __half*>(&u0);
+    const __half* xv1 = reinterpret_cast<const __half*>(&u1);
+    const uint16_t* sv0 = reinterpret_cast<const uint16_t*>(&s0);
+    const uint16_t* sv1 = reinterpret_cast<const uint16_t*>(&s1);
+    const uint16_t* zv0 = reinterpret_cast<const uint16_t*>(&z0);
+    const uint16_t* zv1 = reinterpret_cast<const uint16_t*>(&z1);
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      w0 |= pc_code(__half2float(xv0[k]), half_bits_to_float(sv0[k]), half_bits_to_float(zv0[k])) << (4 * k);
+      w1 |= pc_code(__half2float(xv1[k]), half_bits_to_float(sv1[k]), half_bits_to_float(zv1[k])) << (4 * k);
+    }
+    *reinterpret_cast<uint2*>(packed + (h * s_cap + pos + t) * (D / 2) + 8 * g) = make_uint2(w0, w1);
+  }
+}
+
+template <int D>
+int launch_pc_codes(const __half* x, int64_t xh, int64_t xt, int64_t heads, int64_t ntok,
+                    const uint16_t* scale, const uint16_t* zero, uint8_t* packed, int64_t s_cap,
+                    int64_t pos, cudaStream_t st) {
+  const int64_t total = heads * ntok * (D / 16);
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148LL * 32);
+  pc_codes_vec_kernel<D><<<(unsigned)blocks, 256, 0, st>>>(x, xh, xt, heads, ntok, scale, zero, D, packed,
+                                                           s_cap, pos);
+  return launch_status();
+}
+
+int launch_pc_codes_any(int D, const __half* x, int64_t xh, int64_t xt, int64_t heads, int64_t ntok,
+                        const uint16_t* scale, const uint16_t* zero, uint8_t* packed, int64_t s_cap,
+                        int64_t pos, cudaStream_t st) {
+  if (D == 64) return launch_pc_codes<64>(x, xh, xt, heads, ntok, scale, zero, packed, s_cap, pos, st);
+  if (D == 80) return launch_pc_codes<80>(x, xh, xt, heads, ntok, scale, zero, packed, s_cap, pos, st);
+  return launch_pc_codes<128>(x, xh, xt, heads, ntok, scale, zero, packed, s_cap, pos, st);
+}
+
+// 16-byte-aligned rows, rulers and packed codes (the vector kernels' needs).
+bool pc_vec_ok(const void* x, int64_t xh, int64_t xt, const void* scale, const void* zero,
+               const void* packed, int64_t s_cap, int64_t pos, int64_t D) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scale) |
+                      reinterpret_cast<uintptr_t>(zero);
+  return a % 16 == 0 && (xh * 2) % 16 == 0 && (xt * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(packed) % 8 == 0 &&
+         ((s_cap * (D / 2)) % 8 == 0) && ((pos * (D / 2)) % 8 == 0);
+}
+
 }  // namespace slmt
 
 using namespace slmt;
@@ -246,16 +395,29 @@ extern "C" int slmt_per_channel_quantize(const void* x, int x_dtype,
   const int64_t rows = num_seqs * num_kv_heads;
   if (rows > 65535LL * 32768LL) return SLMT_ERR_SHAPE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const __half* xh = reinterpret_cast<const __half*>(x);
+  if (pc_vec_ok(x, seq_len * head_dim, head_dim, scale, zero, packed, seq_len, 0, head_dim) &&
+      rows * kPcSplit <= (int64_t)INT32_MAX) {
+    const unsigned grid = (unsigned)(rows * kPcSplit);
+    if (head_dim == 64)
+      pc_rulers_vec_kernel<64><<<grid, 256, 0, st>>>(xh, seq_len, scale, zero);
+    else if (head_dim == 80)
+      pc_rulers_vec_kernel<80><<<grid, 256, 0, st>>>(xh, seq_len, scale, zero);
+    else
+      pc_rulers_vec_kernel<128><<<grid, 256, 0, st>>>(xh, seq_len, scale, zero);
+    int rc = launch_status();
+    if (rc != SLMT_OK) return rc;
+    return launch_pc_codes_any((int)head_dim, xh, seq_len * head_dim, head_dim, rows, seq_len, scale, zero,
+                               packed, seq_len, 0, st);
+  }
   const dim3 g1((unsigned)rows, (unsigned)((head_dim + 31) / 32));
-  pc_rulers_kernel<<<g1, 256, 0, st>>>(reinterpret_cast<const __half*>(x), seq_len,
-                                       (int)head_dim, scale, zero);
+  pc_rulers_kernel<<<g1, 256, 0, st>>>(xh, seq_len, (int)head_dim, scale, zero);
   int rc = launch_status();
   if (rc != SLMT_OK) return rc;
   const int64_t total = rows * seq_len * (head_dim / 2);
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148LL * 16);
-  pc_codes_kernel<<<(unsigned)blocks, 256, 0, st>>>(
-      reinterpret_cast<const __half*>(x), seq_len * head_dim, head_dim, rows, seq_len,
-      (int)head_dim, scale, zero, head_dim, packed, seq_len, 0);
+  pc_codes_kernel<<<(unsigned)blocks, 256, 0, st>>>(xh, seq_len * head_dim, head_dim, rows, seq_len,
+                                                    (int)head_dim, scale, zero, head_dim, packed, seq_len, 0);
   return launch_status();
 }
 
@@ -274,6 +436,9 @@ extern "C" int slmt_per_channel_append(const void* x, int x_dtype,
   if (num_new == 0) return SLMT_OK;
   if (!x || !packed || !scale || !zero) return SLMT_ERR_NULL;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pc_vec_ok(x, x_head_stride, x_token_stride, scale, zero, packed, s_cap, pos, head_dim))
+    return launch_pc_codes_any((int)head_dim, reinterpret_cast<const __half*>(x), x_head_stride, x_token_stride,
+                               num_kv_heads, num_new, scale, zero, packed, s_cap, pos, st);
   const int64_t total = num_kv_heads * num_new * (head_dim / 2);
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148LL * 16);
   pc_codes_kernel<<<(unsigned)blocks, 256, 0, st>>>(
