@@ -19,14 +19,16 @@
 //                 P' = p*v_step -> fp16 -> movmatrix -> B operand
 //                 O^T[D x 8 heads] += codes(V)^T . P'^T            (m16n8k16)
 //                 sum_v += p*v_min
-//               4-bit codes go straight from shared memory to exact fp16
-//               integers in registers; no dequantised K/V exists anywhere.
+//               4-bit codes go straight from shared memory to biased fp16
+//               operands in registers (1024+c, 64+c; the bias is taken off
+//               per dot product); no dequantised K/V exists anywhere.
 //   At a segment end: a segment that one CTA streamed alone is normalised and
 //   written straight to the output; otherwise each consumer warp writes
-//   (m, l, acc) to the split-K scratch slot cta+segment, the CTA counts itself
-//   in the segment's arrival counter, and the last CTA to arrive merges all
-//   partials (log-sum-exp weights), writes the output rows and resets the
-//   counter -- no separate combine launch.
+//   (m, l, acc) to the split-K scratch slot cta+segment and the CTA counts
+//   itself in the segment's arrival word.  After their ranges, the CTAs whose
+//   ranges end inside the segment wait for every covering CTA to publish and
+//   each merges a slice of its output rows (log-sum-exp weights); the last
+//   of them resets the word -- no separate combine launch.
 #pragma once
 
 #include "decode_common.cuh"
