@@ -42,7 +42,7 @@ SEQS_PER_GPU = 64
 HQ, HKV, D, BS = 32, 8, 128, 16
 LMIN, LMAX = 128, 8192
 SEED = 1234
-E2E_GRAPH_STEPS = 8  # e2e steps per captured CUDA graph
+E2E_GRAPH_STEPS = 32  # e2e steps per captured CUDA graph (the first input and last output copy of a graph cannot overlap compute)
 NOMINAL_HBM_GBS = 8000.0
 
 

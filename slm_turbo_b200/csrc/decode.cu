@@ -1,4 +1,6 @@
 // decode.cu -- host launchers (C ABI) of the split-K decode kernels.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "decode_kernels.cuh"
@@ -110,6 +112,46 @@ int current_device_sms(int* device_out) {
 }
 
 namespace {
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (the library links the runtime only).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// Tensor map of packed codes [num_seqs, kv, s_cap, half bytes] (sequence
+// stride seq_stride_rows rows) viewed as 8-byte elements [num_seqs, kv,
+// s_cap*half/8]: the box [1, kvc, 32*half/8] is one 32-token chunk of `kvc`
+// kv heads, i.e. kvc contiguous spans, the x coordinate tok0*half/8 of a
+// chunk start is a multiple of 16 bytes.  False (and the bulk-copy path is
+// used) unless every rule of the tiled copy holds: 16-byte aligned base and
+// strides, box within 256 elements per dimension.
+bool encode_codes_map(CUtensorMap* m, const uint8_t* base, int64_t num_seqs, int64_t kv, int64_t s_cap,
+                      int64_t half, int64_t seq_stride_rows, int kvc) {
+  auto enc = tensor_map_encoder();
+  if (!enc || reinterpret_cast<uintptr_t>(base) % 16 != 0 || half % 8 != 0) return false;
+  if (seq_stride_rows < kv * s_cap || s_cap < 1 || num_seqs < 1 || kvc > kv) return false;
+  const int64_t box_x = kChunkTokens * half / 8;
+  if (box_x > 256 || (kChunkTokens * half) % 16 != 0) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)(s_cap * half / 8), (cuuint64_t)kv, (cuuint64_t)num_seqs};
+  const cuuint64_t strides[2] = {(cuuint64_t)(s_cap * half), (cuuint64_t)(seq_stride_rows * half)};
+  for (cuuint64_t st : strides)
+    if (st % 16 != 0 || st >= (1ull << 40)) return false;
+  const cuuint32_t box[3] = {(cuuint32_t)box_x, (cuuint32_t)kvc, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 struct Geometry {
   int G, nt, kvc, ngroups;
@@ -298,6 +340,8 @@ int contig_decode(int layout, const void* q, int q_dtype, int64_t q_seq_stride,
   p.use_quant = use_quant ? 1 : 0;
   p.contig_bulk_ok = (ka % 16 == 0) && (va % 16 == 0) && ((s_cap * half) % 16 == 0) &&
                      ((kv_seq_stride_rows * half) % 16 == 0);
+  p.tma_tensor = encode_codes_map(&p.tmap_k, k_packed, num_seqs, kv, s_cap, half, kv_seq_stride_rows, geo.kvc) &&
+                 encode_codes_map(&p.tmap_v, v_packed, num_seqs, kv, s_cap, half, kv_seq_stride_rows, geo.kvc);
   // rulers [B, KV, D] fp16: a kv group's rows are one span of kvc*D values
   const bool rul_al = ((reinterpret_cast<uintptr_t>(r0) | reinterpret_cast<uintptr_t>(r1) |
                         reinterpret_cast<uintptr_t>(r2) | reinterpret_cast<uintptr_t>(r3)) % 16 == 0);

@@ -2,6 +2,7 @@
 // in-launch partial merge included) and the host launchers.
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 namespace slmt {
@@ -97,6 +98,12 @@ struct DecodeParams {
   int64_t ruler_seq_stride;
   int use_quant, contig_bulk_ok;
   int rul_bulk;  // per-channel rulers of a kv group: four 16-byte aligned spans
+  // contiguous layouts: K and V codes [B, KV, S*D/2 bytes] as 3-D tensor
+  // maps of 8-byte elements with a box of one chunk of a kv group, so a
+  // chunk's K (or V) rows of every kv head of the group arrive with one
+  // tiled TMA copy; used when tma_tensor is set
+  int tma_tensor;
+  CUtensorMap tmap_k, tmap_v;
   // lengths
   const int32_t* seq_lens;
   int seq_len_scalar, causal_rows, len_cap;

@@ -172,7 +172,7 @@ struct StageView {
   static constexpr int d16 = 16 * kRow;
   static constexpr int r8 = (LAYOUT == LAYOUT_PAGED) ? d8 : 8 * KVC * 8;
   static constexpr int r16 = (LAYOUT == LAYOUT_PAGED) ? d16 : 16 * KVC * 8;
-  const uint8_t* base;  // paged: st + j*(D+8); contiguous: st + j*32*D
+  const uint8_t* base;  // paged: st + j*(D+8); contiguous: st + j*32*(D/2) (the K block)
   const uint8_t* rul;   // contiguous per-token rulers: st + KVC*32*D + j*8
   __device__ __forceinline__ const uint8_t* k(int t) const {
     if (LAYOUT == LAYOUT_PAGED) return base + t * kRow;
@@ -180,7 +180,7 @@ struct StageView {
   }
   __device__ __forceinline__ const uint8_t* v(int t) const {
     if (LAYOUT == LAYOUT_PAGED) return base + t * kRow + D / 2;
-    return base + (kChunkTokens / 2) * D + t * (D / 2);
+    return base + KVC * kChunkTokens * (D / 2) + t * (D / 2);  // the V block follows the K block
   }
   __device__ __forceinline__ const uint8_t* rulers(int t) const {
     if (LAYOUT == LAYOUT_PAGED) return base + t * kRow + D;
@@ -426,26 +426,39 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
         if (lane == 0) {
           hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, {0, 0, 0}};
         }
-        const uint32_t tx = bulk ? (uint32_t)(2 * p.kvc * bytes) : 0u;
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(fb, tx);
-        __syncwarp();
-        if (bulk) {
-          if (lane < 2 * p.kvc) {
-            const int jj = lane >> 1, isv = lane & 1;
-            const int64_t roff = (row0 + (int64_t)(kg * p.kvc + jj) * p.s_cap) * HALF;
-            const uint8_t* src = (isv ? p.v_codes : p.k_codes) + roff;
-            bulk_g2s(dst + jj * kChunkTokens * D + isv * (kChunkTokens / 2) * D, src, (uint32_t)bytes, fb,
-                     policy);
+        // stage: K block [kvc][32 rows][D/2] then V block of the same shape
+        const int kblock = p.kvc * kChunkTokens * HALF;
+        if (p.tma_tensor) {
+          // one tiled copy per K / V: the chunk's 32 rows of every kv head of
+          // the group (rows past the capacity arrive as zeros, past the
+          // length as whatever is stored there; both are masked)
+          __syncwarp();
+          if (lane == 0) {
+            const int x0 = tok0 * HALF / 8;  // 8-byte elements
+            mbar_arrive_expect_tx(fb, (uint32_t)(2 * kblock));
+            tma_load_3d(dst, &p.tmap_k, x0, kg * p.kvc, s, fb);
+            tma_load_3d(dst + kblock, &p.tmap_v, x0, kg * p.kvc, s, fb);
           }
         } else {
-          const int cpr = bytes / 8;
-          for (int i = lane; i < 2 * p.kvc * cpr; i += 32) {
-            const int cp = i / cpr, cc = i % cpr;
-            const int jj = cp >> 1, isv = cp & 1;
-            const int64_t roff = (row0 + (int64_t)(kg * p.kvc + jj) * p.s_cap) * HALF + cc * 8;
-            cp_async8(dst + jj * kChunkTokens * D + isv * (kChunkTokens / 2) * D + cc * 8,
-                      (isv ? p.v_codes : p.k_codes) + roff);
+          const uint32_t tx = bulk ? (uint32_t)(2 * p.kvc * bytes) : 0u;
+          __syncwarp();
+          if (lane == 0) mbar_arrive_expect_tx(fb, tx);
+          __syncwarp();
+          if (bulk) {
+            if (lane < 2 * p.kvc) {
+              const int jj = lane >> 1, isv = lane & 1;
+              const int64_t roff = (row0 + (int64_t)(kg * p.kvc + jj) * p.s_cap) * HALF;
+              const uint8_t* src = (isv ? p.v_codes : p.k_codes) + roff;
+              bulk_g2s(dst + isv * kblock + jj * kChunkTokens * HALF, src, (uint32_t)bytes, fb, policy);
+            }
+          } else {
+            const int cpr = bytes / 8;
+            for (int i = lane; i < 2 * p.kvc * cpr; i += 32) {
+              const int cp = i / cpr, cc = i % cpr;
+              const int jj = cp >> 1, isv = cp & 1;
+              const int64_t roff = (row0 + (int64_t)(kg * p.kvc + jj) * p.s_cap) * HALF + cc * 8;
+              cp_async8(dst + isv * kblock + jj * kChunkTokens * HALF + cc * 8, (isv ? p.v_codes : p.k_codes) + roff);
+            }
           }
         }
       }
@@ -1076,7 +1089,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
         sv.base = st + j * (D + 8);
         sv.rul = nullptr;
       } else {
-        sv.base = st + j * kChunkTokens * D;
+        sv.base = st + j * kChunkTokens * (D / 2);
         sv.rul = st + kvc * kChunkTokens * D + j * 8;
       }
       // a segment's last chunk keeps its stage (and descriptor) until the
@@ -1232,7 +1245,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 // about 9 with two n-tiles.
 template <int D, int NT, int LAYOUT, int KVC, bool PK>
 __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
-    decode_splitk_kernel(const DecodeParams p) {
+    decode_splitk_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   SmemHeader* hdr = reinterpret_cast<SmemHeader*>(smem);
   uint8_t* qbuf = smem + kHeaderBytes;

@@ -89,6 +89,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src,
       : "memory");
 }
 
+// Tiled 3-D TMA copy global -> shared of the box at (c0, c1, c2) of the
+// tensor map `tmap` (the address of a __grid_constant__ kernel parameter),
+// completing the box's bytes of tx on `bar`.  c0 (the innermost coordinate)
+// times the element size is a multiple of 16 bytes.  No multicast.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // L2 policy for data streamed once (the packed cache).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t p;
