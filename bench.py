@@ -8,15 +8,19 @@ Workload per GPU (weak scaling): 64 sequences of a global ragged batch of
 longest-first bin packing on token count; Hq=32, Hkv=8, D=128, block_size 16,
 pages randomly permuted in a pool sized to the tokens, int32 block tables,
 K/V ~ N(0,1) fp16 quantized into the pool by the store kernel.  One step =
-append 1 new token per sequence (kv_quantize_store) + ragged decode of every
-sequence (one split-K launch that also merges the partials), i.e. one
-attention layer of one decode step.  The pool (~290 MB/GPU) is larger than L2, so no flush is needed.
+append 1 new token per sequence + ragged decode of every sequence, as ONE
+launch (kv_append_decode_paged_batched: the split-K decode kernel quantizes
+each sequence's new token itself and merges the partials in the same
+launch), i.e. one attention layer of one decode step.  The pool (~290
+MB/GPU) is larger than L2, so no flush is needed.
 
 Reported: tok/s (sequences decoded per second, all GPUs), µs/step, the
 decode kernel's algorithmic HBM GB/s against MEASURED_PEAKS.json, an
 end-to-end figure through the public Python API with pinned host buffers,
 and the CPU oracle timed on this host.  ``--impl reference`` times the
-reference path's CPU restatement (oracle/kvq_oracle.c) on the same workload.
+reference path's CPU restatement (oracle/kvq_oracle.c) on the same workload,
+and beside it the reference's own CUDA kernels (its extension built
+unmodified into oracle/_ref) driven as its vLLM adapter drives them.
 """
 from __future__ import annotations
 
@@ -43,6 +47,8 @@ HQ, HKV, D, BS = 32, 8, 128, 16
 LMIN, LMAX = 128, 8192
 SEED = 1234
 E2E_GRAPH_STEPS = 32  # e2e steps per captured CUDA graph (the first input and last output copy of a graph cannot overlap compute)
+DECODE_LAUNCHES = 2000  # decode-only launches timed back to back for the roofline (whatever --steps is)
+E2E_EAGER_STEPS = 500  # e2e steps issued eagerly through the public API
 NOMINAL_HBM_GBS = 8000.0
 
 
@@ -98,8 +104,10 @@ def step_slots(w):
 
 
 def algorithmic_bytes(w):
-    """Bytes the decode kernel must move (SURVEY 8(d) C3 formula): packed slots
-    of every context token and kv head, block-table entries, q in, out (fp32)."""
+    """Bytes the decode kernel must move: the packed slot of every context
+    token and kv head (D/2 K + D/2 V + 8 ruler bytes), one 4-byte block-table
+    entry per page, q in (fp16) and out (fp32) per query head, and the
+    sequence lengths; plus the store's bytes (new K/V in, slots out)."""
     toks = int(w["seq_lens1"].sum())
     pages = sum((L + BS - 1) // BS for L in w["seq_lens1"].tolist())
     B = len(w["lengths"])
@@ -140,7 +148,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            time.sleep(0.005)
+            time.sleep(0.002)
 
     def __enter__(self):
         if self._h is not None:
@@ -300,8 +308,71 @@ def run_reference(args):
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": nthreads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    try:
+        line["reference_cuda_same_box"] = reference_cuda_same_box(w, args.steps, args.warmup)
+    except Exception as exc:  # a report beside the CPU arm, never a reason to fail it
+        line["reference_cuda_same_box"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_cuda_same_box(w, steps, warmup):
+    """The reference's own CUDA kernels (its extension, built unmodified into
+    oracle/_ref) on this GPU, driven as its vLLM adapter drives them for one
+    decode step of one layer: kv_quantize_store_cuda for the step's tokens
+    (adapters/vllm_adapter.py:185-203), then seq_lens.tolist() and one
+    kv_dequant_decode_per_token_paged_attention_cuda launch per request
+    (:246-284).  Pool filled by the reference's own store kernel.  Timed with
+    CUDA events around whole steps, host loop included."""
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    from oracle.build_ref import load_ref
+    ref = load_ref()
+    if ref is None:
+        return {"unavailable": "reference extension not built into oracle/_ref"}
+    _, _, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B = len(w["lengths"])
+    bt = w["block_tables"].to(torch.int64)
+    cache = torch.zeros(w["num_blocks"], BS, HKV, D + 8, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(SEED + 7)
+    for i, L in enumerate(w["lengths"]):
+        t = torch.arange(L)
+        slots = (bt[i, t // BS] * BS + t % BS).to(dev)
+        k = torch.randn(L, HKV, D, device=dev, generator=g, dtype=torch.float32).half()
+        v = torch.randn(L, HKV, D, device=dev, generator=g, dtype=torch.float32).half()
+        ref.kv_quantize_store_cuda(k, v, cache, slots, BS)
+    q = torch.randn(B, HQ, D, device=dev, generator=g).half()
+    k_new = torch.randn(B, HKV, D, device=dev, generator=g).half()
+    v_new = torch.randn(B, HKV, D, device=dev, generator=g).half()
+    slots_d = step_slots(w).to(dev)
+    sl_d = w["seq_lens1"].to(dev)
+    rows = [bt[r].to(dev).contiguous() for r in range(B)]
+    out = torch.empty(B, HQ, D, dtype=torch.float16, device=dev)
+
+    def step():
+        ref.kv_quantize_store_cuda(k_new, v_new, cache, slots_d, BS)
+        for r, L in enumerate(sl_d.tolist()):
+            o = ref.kv_dequant_decode_per_token_paged_attention_cuda(
+                q[r:r + 1].permute(1, 0, 2).contiguous(), cache, rows[r], int(L), BS, HKV)
+            out[r] = o.permute(1, 0, 2)[0]
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    n = max(steps, 5)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / n
+    return {"value": B / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms, "steps": n,
+            "mode": "reference CUDA kernels (oracle/_ref, built unmodified for sm_100a) on this GPU: one "
+                    "store launch + seq_lens.tolist() + one decode launch per request, as the reference "
+                    "adapter runs a decode step"}
 
 
 def run_ours(args):
@@ -324,7 +395,6 @@ def run_ours(args):
     B = len(lengths)
     bt_d = w["block_tables"].to(dev)
     sl_d = w["seq_lens1"].to(dev)
-    slots_d = step_slots(w).to(dev)
     g = torch.Generator(device=dev).manual_seed(SEED + 11 + rank)
     q = torch.randn(B, HQ, D, device=dev, generator=g).half()
     k_new = torch.randn(B, HKV, D, device=dev, generator=g).half()
@@ -333,8 +403,7 @@ def run_ours(args):
     maxlen = int(w["seq_lens1"].max())
 
     def step():
-        kd.kv_quantize_store(k_new, v_new, cache, slots_d, BS)
-        kd.kv_decode_paged_batched(q, cache, bt_d, sl_d, out=out, max_seq_len=maxlen)
+        kd.kv_append_decode_paged_batched(q, k_new, v_new, cache, bt_d, sl_d, out=out, max_seq_len=maxlen)
 
     def decode_only():
         kd.kv_decode_paged_batched(q, cache, bt_d, sl_d, out=out, max_seq_len=maxlen)
@@ -360,36 +429,38 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
+    clk = ClockSampler(dev.index)
+    clk.__enter__()  # sampled across the K steps and the decode-only leg below
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
     barrier()
     ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
 
-    # ---- dominant kernel: the decode launch alone, per launch ----
-    n_dec = max(args.steps, 20)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_dec)]
-    for a, b in evs:
-        a.record(stream)
+    # ---- dominant kernel: the decode launch alone, DECODE_LAUNCHES back to back ----
+    n_dec = max(DECODE_LAUNCHES, args.steps)
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    for _ in range(n_dec):
         decode_only()
-        b.record(stream)
+    d1.record(stream)
     torch.cuda.synchronize(dev)
-    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    dec_ms = max_over_ranks(dec_ms)
+    clk.__exit__()
+    dec_ms = max_over_ranks(d0.elapsed_time(d1) / n_dec)
     dec_bytes, store_bytes = algorithmic_bytes(w)
     peak, peak_src = measured_peak()
     achieved = dec_bytes / (dec_ms * 1e-3) / 1e9
 
     # ---- end to end through the public API with pinned host buffers ----
-    # Each step's inputs (q, new K/V, slots, lengths) travel in ONE pinned
-    # host -> device copy and its fp32 output in one device -> host copy, on
-    # their own copy streams, double-buffered: the input copy of step t+1 and
-    # the output copy of step t-1 run while step t computes, as a serving
-    # loop would run them.
-    h_parts = [q.cpu(), k_new.cpu(), v_new.cpu(), step_slots(w), w["seq_lens1"]]
+    # Each step's inputs (q, new K/V, lengths) travel in ONE pinned host ->
+    # device copy and its fp32 output in one device -> host copy, on their
+    # own copy streams, double-buffered: the input copy of step t+1 and the
+    # output copy of step t-1 run while step t computes, as a serving loop
+    # would run them.  The page pool and the block tables are the engine's
+    # resident state and stay on the device.
+    h_parts = [q.cpu(), k_new.cpu(), v_new.cpu(), w["seq_lens1"]]
     offs, o = [], 0
     for t in h_parts:
         offs.append(o)
@@ -438,9 +509,8 @@ def run_ours(args):
             cs.wait_event(ev_in[sl])
             if i >= 2:
                 cs.wait_event(ev_out[sl])  # slot's previous output read out
-            dq, dk, dv, dslots, dsl = d_views[sl]
-            kd.kv_quantize_store(dk, dv, cache, dslots, BS)
-            kd.kv_decode_paged_batched(dq, cache, bt_d, dsl, out=d_out[sl], max_seq_len=maxlen)
+            dq, dk, dv, dsl = d_views[sl]
+            kd.kv_append_decode_paged_batched(dq, dk, dv, cache, bt_d, dsl, out=d_out[sl], max_seq_len=maxlen)
             ev_done[sl].record(cs)
             with torch.cuda.stream(d2h_stream):
                 d2h_stream.wait_event(ev_done[sl])
@@ -449,11 +519,25 @@ def run_ours(args):
         cs.wait_stream(h2d_stream)
         cs.wait_stream(d2h_stream)
 
-    # The steps are replayed from a CUDA graph of E2E_GRAPH_STEPS pipelined
-    # steps (the public API calls captured once), as a serving engine runs
-    # decode; the host then issues one graph launch per E2E_GRAPH_STEPS steps.
+    # (a) eager: the public API called once per step from Python, as a
+    # serving loop without CUDA graphs calls it
     e2e_run(4)
     torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_eager = max(E2E_EAGER_STEPS, args.steps)
+    e0.record(stream)
+    e2e_run(n_eager)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_eager_ms = max_over_ranks(e0.elapsed_time(e1) / n_eager)
+    assert torch.equal(h_out[(n_eager - 1) & 1], d_out[(n_eager - 1) & 1].cpu()), "e2e output copy mismatch"
+
+    # (b) the same steps replayed from a CUDA graph of E2E_GRAPH_STEPS
+    # pipelined steps (the public API calls captured once), as a serving
+    # engine runs decode; the host issues one graph launch per
+    # E2E_GRAPH_STEPS steps.
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         e2e_run(E2E_GRAPH_STEPS)
@@ -461,7 +545,6 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     barrier()
     n_rep = max(1, args.steps // E2E_GRAPH_STEPS)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(n_rep):
         graph.replay()
@@ -496,18 +579,25 @@ def run_ours(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic", "config": workload_config(w, world),
         "decode_us": dec_ms * 1e3, "decode_hbm_gbs": achieved,
+        "step": "one launch: new token quantized into the cache + decode (append fused)",
         "hbm_pct_of_8tbs": 100.0 * achieved / NOMINAL_HBM_GBS,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": profiled_traffic(dec_bytes),
-                     "kernel": "decode_splitk_kernel<128,1,PAGED,8> (partials merged inside the launch)",
-                     "algorithmic_bytes_per_launch": dec_bytes, "peak_source": peak_src},
+                     "kernel": "decode_splitk_kernel<128,1,PAGED,8,PK> (partials merged inside the launch)",
+                     "algorithmic_bytes_per_launch": dec_bytes, "peak_source": peak_src,
+                     "timing": f"{n_dec} decode-only launches back to back between two CUDA events"},
         "e2e": {"value": total_seqs / (e2e_ms * 1e-3),
                 "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "mode": f"public API captured as a CUDA graph of {E2E_GRAPH_STEPS} steps; per step one "
-                        "pinned H2D of the inputs and one D2H of the fp32 output, each on its own copy "
-                        "stream, double-buffered against the compute",
-                "ms_per_step": e2e_ms},
-        "gpu_launches": 2 * args.steps,  # kv_store_kernel + decode_splitk_kernel per step
+                "mode": f"public API (kv_append_decode_paged_batched) captured as a CUDA graph of "
+                        f"{E2E_GRAPH_STEPS} steps; per step one pinned H2D of q, new K/V and lengths and "
+                        "one D2H of the fp32 output, each on its own copy stream, double-buffered against "
+                        "the compute; the page pool and block tables stay resident on the device",
+                "ms_per_step": e2e_ms,
+                "eager": {"value": total_seqs / (e2e_eager_ms * 1e-3), "unit": "tok/s",
+                          "ms_per_step": e2e_eager_ms,
+                          "mode": f"the same {n_eager} steps issued eagerly, one public-API call per step "
+                                  "from Python (no CUDA graph)"}},
+        "gpu_launches": args.steps,  # one decode_splitk_kernel (append fused) per step
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }

@@ -72,6 +72,27 @@ const char* slmt_status_string(int status);
 int slmt_device_sm_count(int device);
 
 /*
+ * Bound of every wait inside the decode kernels (pipeline barriers, the
+ * split-K merge's wait for the other CTAs of a segment), in nanoseconds, for
+ * launches issued after the call; ns <= 0 restores the default of 4 s.  A
+ * wait that runs out sets SLMT_DEVERR_TIMEOUT in *err_flag and the kernel
+ * returns (after its in-flight copies landed) instead of hanging; its
+ * outputs are then undefined and the workspace must be zeroed again.
+ * Process-wide; returns the previous value.  No counterpart in the reference
+ * (its kernels have no waits).
+ */
+int64_t slmt_set_wait_limit_ns(int64_t ns);
+
+/*
+ * Test hook for failure detection, off by default: while on, the consumer
+ * warps of CTA 0 of every decode launch wait on a barrier that nothing
+ * completes, so that wait runs out after the wait limit above and the launch
+ * reports SLMT_DEVERR_TIMEOUT without faulting or hanging.  Process-wide;
+ * returns the previous setting.  No counterpart in the reference.
+ */
+int slmt_set_debug_stall(int on);
+
+/*
  * Bytes of split-K scratch the decode entry points need for `num_seqs`
  * sequences (pseudo-sequences for prefill) on `device`; negative on error.
  * The first workspace_bytes/64 bytes (rounded up to 256) of the scratch hold
@@ -133,6 +154,42 @@ int slmt_paged_decode(const void* q, int q_dtype, int64_t q_seq_stride,
                       int64_t out_head_stride, void* workspace,
                       int64_t workspace_bytes, int32_t* err_flag,
                       void* stream);
+
+/*
+ * One decode step of a ragged batch in ONE launch: each sequence's new token
+ * is quantized into the paged cache and then every sequence is decoded over
+ * its whole context, the new token included.  new_key/new_value: [num_seqs,
+ * num_kv_heads, head_dim] fp16 or bf16 (kv_dtype), head rows contiguous,
+ * sequence stride new_seq_stride elements.  seq_lens (required) are the
+ * lengths AFTER the append: the new token of sequence b goes to position
+ * seq_lens[b]-1, i.e. slot block_tables[b][(len-1)/block_size]*block_size +
+ * (len-1)%block_size, the slot vLLM's slot_mapping names for a decode token.
+ * A sequence of length 0 appends nothing and produces zeros.  The slot's
+ * bytes are those slmt_kv_quantize_store writes for the same row, and the
+ * outputs are those of slmt_kv_quantize_store followed by slmt_paged_decode.
+ * The warp that decodes a sequence's final chunk quantizes its kv head's new
+ * row, so no separate store launch and no re-read of the new slot from HBM.
+ * Every other argument as slmt_paged_decode.
+ * ref: the decode step of adapters/vllm_adapter.py (do_kv_cache_update
+ *      :185-203 then _decode_attention :246-284), i.e. kv_quantize_store_cuda
+ *      (kernels/kv_dequant_cuda.cu:415-456) followed by one
+ *      kv_dequant_decode_per_token_paged_attention_cuda (.cu:355-410) per
+ *      request.
+ */
+int slmt_paged_append_decode(const void* q, int q_dtype, int64_t q_seq_stride,
+                             int64_t q_head_stride, const void* new_key,
+                             const void* new_value, int kv_dtype,
+                             int64_t new_seq_stride, uint8_t* kv_cache,
+                             int64_t num_blocks, int64_t block_size,
+                             int64_t num_kv_heads, int64_t head_dim,
+                             const void* block_tables, int bt_dtype,
+                             int64_t bt_seq_stride, int64_t max_blocks_per_seq,
+                             const int32_t* seq_lens, int64_t max_seq_len_hint,
+                             int64_t num_seqs, int64_t num_q_heads, float sm_scale,
+                             void* out, int out_dtype, int64_t out_seq_stride,
+                             int64_t out_head_stride, void* workspace,
+                             int64_t workspace_bytes, int32_t* err_flag,
+                             void* stream);
 
 /*
  * Batched decode attention over the standalone per-channel layout.
@@ -240,13 +297,16 @@ int slmt_per_channel_append(const void* x, int x_dtype, int64_t x_head_stride,
  * sequences at 32 query heads x 128 dims on a 148-SM device.
  * Zero state: the array starts zero-filled when the module loads.  Its first
  * 1/64 holds arrival counters that must be zero when a launch starts; each
- * launch that completes without a device error bit leaves them at zero.  After a call that set a bit in *err_flag, pass
- * reset_scratch != 0 on the next call: that zeroes the counters with
- * cudaMemsetAsync on `stream` before the launch (0 skips it).
+ * launch that completes without a device error bit leaves them at zero.
+ * After a call that set a bit in *err_flag, pass reset_scratch != 0 on the
+ * next call: that zeroes the counters with cudaMemsetAsync on `stream`
+ * before the launch (0 skips it).
  * Set-up: the first call on each device (with that device current) looks up
  * the array's address with cudaGetSymbolAddress, which may load the module,
  * and the first decode call configures the kernel; make that first call
- * before any stream capture begins.
+ * before any stream capture begins.  The address is cached per device for
+ * the life of the process, which assumes the device's primary context lives
+ * as long (no cudaDeviceReset in between).
  * Concurrency: all calls on one device share the one array, so two calls
  * whose executions overlap (different streams, or different host threads)
  * race on it and give wrong results; order them on one stream or with

@@ -1,6 +1,7 @@
 """Compile the REFERENCE's own CUDA extension into ``oracle/_ref/`` (checker only).
 
-    python -m oracle.build_ref [/path/to/slm-turbo]
+    python -m oracle.build_ref /path/to/slm-turbo
+    SLMT_REFERENCE_TREE=/path/to/slm-turbo python -m oracle.build_ref
 
 Builds kernels/kv_dequant_cuda.cu (+ kv_dequant_kernels.cuh) of the slm-turbo
 tree where it lies, unmodified, for sm_100a, with the same flags its JIT
@@ -14,6 +15,7 @@ from __future__ import annotations
 
 import importlib.machinery
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -27,12 +29,26 @@ def built_path():
     return cands[0] if cands else None
 
 
-def build_ref(ref_root: str = "/root/reference", force: bool = False):
-    """Build (or reuse) the reference extension; returns its path or None."""
+def reference_tree(arg=None):
+    """The slm-turbo source tree to build from: the argument, else the
+    SLMT_REFERENCE_TREE environment variable; None when neither names an
+    existing directory (there is no default location)."""
+    cand = arg or os.environ.get("SLMT_REFERENCE_TREE")
+    if cand and Path(cand).is_dir():
+        return Path(cand)
+    return None
+
+
+def build_ref(ref_root=None, force: bool = False):
+    """Build (or reuse) the reference extension; returns its path or None
+    (None also when no reference tree is given and none was built before)."""
     so = built_path()
     if so is not None and not force:
         return so
-    src = Path(ref_root) / "kernels" / "kv_dequant_cuda.cu"
+    root = reference_tree(ref_root)
+    if root is None:
+        return None
+    src = root / "kernels" / "kv_dequant_cuda.cu"
     if not src.exists():
         return None
     from torch.utils.cpp_extension import load
@@ -57,4 +73,5 @@ def load_ref():
 
 
 if __name__ == "__main__":
-    print(build_ref(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", force="--force" in sys.argv))
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    print(build_ref(args[0] if args else None, force="--force" in sys.argv))

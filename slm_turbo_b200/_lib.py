@@ -24,12 +24,17 @@ SIGNATURES = {
     "slmt_version": (_i32, []),
     "slmt_status_string": (ctypes.c_char_p, [_i32]),
     "slmt_device_sm_count": (_i32, [_i32]),
+    "slmt_set_wait_limit_ns": (_i64, [_i64]),
+    "slmt_set_debug_stall": (_i32, [_i32]),
     "slmt_decode_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _i32]),
     "slmt_kv_quantize_store": (_i32, [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp,
                                       _vp]),
     "slmt_paged_decode": (_i32, [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i64, _i64,
                                  _vp, _i64, _i64, _i64, _i64, _f32, _vp, _i32, _i64, _i64, _vp, _i64, _vp,
                                  _vp]),
+    "slmt_paged_append_decode": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _i64, _i64, _i64, _i64,
+                                        _vp, _i32, _i64, _i64, _vp, _i64, _i64, _i64, _f32, _vp, _i32, _i64,
+                                        _i64, _vp, _i64, _vp, _vp]),
     "slmt_paged_decode_noalloc": (_i32, [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i64,
                                          _i64, _vp, _i64, _i64, _i64, _i64, _f32, _vp, _i32, _i64, _i64, _i32,
                                          _vp, _vp]),
@@ -97,8 +102,13 @@ def dtype_tag(dt: torch.dtype) -> int:
 class _DeviceState:
     def __init__(self, device: torch.device):
         self.device = device
-        self.workspace = torch.empty(0, dtype=torch.uint8, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        # split-K scratch per CUDA stream: calls that may overlap on the GPU
+        # (different streams) never share arrival counters
+        self.workspaces: dict = {}
+        # buffers replaced by a larger one stay allocated for the life of the
+        # process: a CUDA graph captured with the old buffer keeps using it
+        self.retired: list = []
 
 
 _states: dict = {}
@@ -117,10 +127,13 @@ _ws_need: dict = {}
 
 
 def workspace(device: torch.device, num_seqs: int, hq: int, kv: int, d: int) -> torch.Tensor:
-    """Split-K scratch for a decode call (grown, never shrunk, per device).
+    """Split-K scratch for a decode call on the current stream of `device`.
 
-    Allocated zero-filled: it holds the per-segment arrival counters, which
-    the kernel leaves at zero after every complete call."""
+    One buffer per (device, stream), grown (to the next power of two of the
+    bytes needed) and never shrunk or freed: a larger request retires the
+    old buffer, which stays allocated so that a CUDA graph captured with it
+    replays safely.  Allocated zero-filled: it holds the per-segment arrival
+    counters, which every complete call leaves at zero again."""
     st = device_state(device)
     key = (st.device.index, num_seqs, hq, kv, d)
     need = _ws_need.get(key)
@@ -128,9 +141,15 @@ def workspace(device: torch.device, num_seqs: int, hq: int, kv: int, d: int) -> 
         need = int(load().slmt_decode_workspace_bytes(num_seqs, hq, kv, d, st.device.index))
         check(need if need < 0 else 0, "slmt_decode_workspace_bytes")
         _ws_need[key] = need
-    if st.workspace.numel() < need:
-        st.workspace = torch.zeros(need, dtype=torch.uint8, device=st.device)
-    return st.workspace
+    stream = torch.cuda.current_stream(st.device).cuda_stream
+    ws = st.workspaces.get(stream)
+    if ws is None or ws.numel() < need:
+        if ws is not None:
+            st.retired.append(ws)
+        size = 1 << max(need - 1, 1).bit_length()
+        ws = torch.zeros(size, dtype=torch.uint8, device=st.device)
+        st.workspaces[stream] = ws
+    return ws
 
 
 def error_word(device: torch.device) -> torch.Tensor:
@@ -141,10 +160,12 @@ def read_device_errors(device, reset: bool = True) -> int:
     """Synchronise and return the kernels' error bits (SLMT_DEVERR_*).
 
     After an error the scratch counters may be left non-zero by an aborted
-    launch, so the workspace is zeroed again together with the error word."""
+    launch, so every workspace of the device is zeroed again together with
+    the error word."""
     st = device_state(torch.device(device))
     v = int(st.err.item())
     if reset and v:
         st.err.zero_()
-        st.workspace.zero_()
+        for ws in list(st.workspaces.values()) + st.retired:
+            ws.zero_()
     return v

@@ -8,14 +8,33 @@ bytes, ``TQFullAttentionSpec``), the same cache shape
 ``(num_blocks, block_size, num_kv_heads, head_size + 8)`` uint8, the same
 quantize-on-write in ``do_kv_cache_update`` and the same SDPA prefill.
 
-What changes is the decode: the reference loops over requests in Python,
-syncs ``seq_lens.tolist()`` and launches one single-request kernel per
-request per layer (adapters/vllm_adapter.py:246-284).  Here one launch
-decodes the whole batch straight from ``attn_metadata.block_table`` (int32)
-and ``attn_metadata.seq_lens`` on the device and writes the output rows in
-the query dtype -- no host sync, so the step is CUDA-graph capturable.  The
-softmax scale stays 1/sqrt(head_size), as in the reference kernel
-(kernels/kv_dequant_kernels.cuh:703).
+What changes:
+
+* Decode: the reference loops over requests in Python, syncs
+  ``seq_lens.tolist()`` and launches one single-request kernel per request
+  per layer (adapters/vllm_adapter.py:246-284).  Here one launch decodes the
+  whole batch straight from ``attn_metadata.block_table`` (int32) and
+  ``attn_metadata.seq_lens`` on the device and writes the output rows in the
+  query dtype -- no host sync, so the step is CUDA-graph capturable.
+* Prefill and mixed batches: the reference runs one causal SDPA over the
+  raw K/V of the whole batch as if it were one sequence
+  (adapters/vllm_adapter.py:218-243), so a batch of several prompts attends
+  across requests, and a continuation chunk (chunked prefill, prefix cache)
+  or a decode row in a mixed batch never sees its cached prefix.  Here each
+  request is handled on its own: a request whose tokens are all new (no
+  cached context) gets causal attention over its own raw K/V, exactly the
+  reference's first-chunk computation; every other query token attends to
+  its request's packed cache through the block table (positions 0..its
+  own), with the same kernel as decode.  All of it stays on the device.
+* The impl's ``scale`` is honoured in decode too (the reference kernel hard
+  codes 1/sqrt(head_size), kernels/kv_dequant_kernels.cuh:703; the two agree
+  for the usual models).
+* The kernels' device error word (bad page id, slot beyond the cache, a
+  pipeline wait past its limit) is polled once per step without a sync and
+  raised as ``RuntimeError`` instead of being served as silent wrong output.
+* A process whose kernel library failed to load raises a ``RuntimeError``
+  naming the cause on the first store or attention call (the reference
+  skips the store and then fails on an unset attribute).
 
 The serving lifecycle class of the reference (``SlmTurboVLLMAdapter``,
 lines 359-690) is not part of the kernel path and is not reproduced.
@@ -54,6 +73,7 @@ if VLLM_AVAILABLE:
 
 SUPPORTED_HEAD_SIZES = (64, 80, 128)
 _KERNEL_CALLS = 0
+_PREFILL_ROWS = 1024  # query rows per masked-SDPA block of a first-chunk prefill
 
 QuantizedKVAttentionImpl = None
 QuantizedKVAttentionBackend = None
@@ -91,6 +111,46 @@ def _patch_attention_layer_spec() -> bool:
     return True
 
 
+class _ErrorWatch:
+    """Sync-free poll of the kernels' device error word (SLMT_DEVERR_* bits).
+
+    Each poll reads the word copied at the previous poll once that copy has
+    landed, then queues the next copy into pinned host memory: a bad page id
+    or a timed-out pipeline wait surfaces one step later as RuntimeError."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+
+    def poll(self) -> None:
+        if torch.cuda.is_current_stream_capturing():
+            return
+        from slm_turbo_b200 import _lib
+        if self.event is not None and self.event.query():
+            bits = int(self.host[0])
+            if bits:
+                logger.error("slm-turbo kernels set device error bits 0x%x", bits)
+                raise RuntimeError(f"slm-turbo kernels reported device error bits 0x{bits:x} "
+                                   "(1 bad block id, 2 slot beyond the cache, 4 wait timeout, "
+                                   "8 length above the block table)")
+        self.host.copy_(_lib.error_word(self.device), non_blocking=True)
+        if self.event is None:
+            self.event = torch.cuda.Event()
+        self.event.record()
+
+
+_WATCHES: dict = {}
+
+
+def _error_watch(device: torch.device) -> _ErrorWatch:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    w = _WATCHES.get(key)
+    if w is None:
+        w = _WATCHES[key] = _ErrorWatch(torch.device("cuda", key))
+    return w
+
+
 def _register_custom_backend() -> bool:
     """Define and register the CUSTOM backend (ref :141-323)."""
     global QuantizedKVAttentionImpl, QuantizedKVAttentionBackend  # noqa: PLW0603
@@ -110,6 +170,7 @@ def _register_custom_backend() -> bool:
             super().__init__(*args, **kwargs)
             self._slm_kernel = False
             self._slm_kernel_err: Optional[str] = None
+            self._slm_meta = None  # metadata object of the step being served
             try:
                 from slm_turbo_b200.kernels.kv_dequant import (
                     _load_cuda_extension,
@@ -126,12 +187,17 @@ def _register_custom_backend() -> bool:
                 self._slm_kernel_err = f"{type(e).__name__}: {e}"
             if self._slm_kernel_err:
                 logger.warning("slm-turbo kernel disabled in this process: %s", self._slm_kernel_err)
+                self._slm_decode_batched = self._kernel_unavailable
+                self._slm_store = self._kernel_unavailable
+
+        def _kernel_unavailable(self, *args, **kwargs):
+            # the cache is packed 4-bit: nothing else can write or read it
+            raise RuntimeError(f"slm-turbo 4-bit KV kernels unavailable in this process: "
+                               f"{self._slm_kernel_err}")
 
         def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping):
             """Quantize the batch's K/V into their packed slots (ref :185-203)."""
             if kv_cache is None or kv_cache.numel() == 0:
-                return
-            if not self._slm_kernel:
                 return
             try:
                 self._slm_store(key, value, kv_cache, slot_mapping, kv_cache.shape[1])
@@ -150,39 +216,77 @@ def _register_custom_backend() -> bool:
             n = attn_metadata.num_actual_tokens
             if n <= 0:
                 return output.fill_(0)
+            if attn_metadata is not self._slm_meta:  # first layer of a new step
+                self._slm_meta = attn_metadata
+                _error_watch(query.device).poll()
             q = query[:n]
+            out = output[:n].view(n, self.num_heads, self.head_size)
             if attn_metadata.max_query_len > 1:
-                attn_out = self._prefill_attention(q, key[:n], value[:n], kv_cache, attn_metadata)
-                if output.ndim == 3:
-                    output[:n] = attn_out.to(output.dtype)
-                else:
-                    output[:n] = attn_out.reshape(n, -1).to(output.dtype)
+                self._prefill_attention(q, key[:n], value[:n], kv_cache, attn_metadata, out)
             else:
-                self._decode_attention(q, kv_cache, attn_metadata, output, n)
+                self._decode_attention(q, kv_cache, attn_metadata, out, n)
             return output
 
-        def _prefill_attention(self, query, key, value, kv_cache, attn_metadata):
-            """SDPA on the raw K/V of the batch, as the reference (ref :230-243)."""
-            hq, hk = query.shape[1], key.shape[1]
-            out = torch.nn.functional.scaled_dot_product_attention(
-                query.transpose(0, 1).unsqueeze(0), key.transpose(0, 1).unsqueeze(0),
-                value.transpose(0, 1).unsqueeze(0), is_causal=True, scale=self.scale,
-                enable_gqa=hk < hq)
-            return out[0].transpose(0, 1)
+        def _prefill_attention(self, query, key, value, kv_cache, attn_metadata, out):
+            """Per request: raw-K/V causal attention for a request with no cached
+            context (the reference's first-chunk SDPA, :230-243), the packed
+            cache through the block table for every other query token."""
+            global _KERNEL_CALLS
+            n, hq, d = query.shape
+            dev = query.device
+            qsl = attn_metadata.query_start_loc.to(torch.int64)
+            seq_lens = attn_metadata.seq_lens.to(torch.int64)
+            nreq = seq_lens.shape[0]
+            qsl = qsl[:nreq + 1]
+            tok = torch.arange(n, device=dev)
+            req = torch.searchsorted(qsl[1:], tok, right=True).clamp_(max=max(nreq - 1, 0))
+            ctx = seq_lens - (qsl[1:] - qsl[:-1])       # cached tokens before this step's chunk
+            pos = ctx[req] + (tok - qsl[req])           # absolute position of each query token
+            first = ctx[req] <= 0                       # request with no cached context
+            # every query token with cached context is a pseudo-sequence of
+            # length pos+1 over its request's pages; the others get length 0
+            vlen = torch.where(first, torch.zeros_like(pos), pos + 1).to(torch.int32)
+            bt = attn_metadata.block_table[:nreq].index_select(0, req)
+            self._slm_decode_batched(
+                query, kv_cache, bt, vlen, block_size=kv_cache.shape[1], num_kv_heads=kv_cache.shape[2],
+                out=out, sm_scale=self.scale, max_seq_len=int(attn_metadata.max_seq_len))
+            _KERNEL_CALLS += 1
+            raw = self._first_chunk_attention(query, key, value, req)
+            out.copy_(torch.where(first.view(n, 1, 1), raw.to(out.dtype), out))
+            return out
 
-        def _decode_attention(self, query, kv_cache, attn_metadata, output, n):
+        def _first_chunk_attention(self, query, key, value, req):
+            """Causal attention of each request over its own raw K/V (the
+            reference's prefill restricted to one request), in blocks of
+            query rows so the mask stays small."""
+            n, hq, d = query.shape
+            hk = key.shape[1]
+            if hk != hq:
+                key = key.repeat_interleave(hq // hk, dim=1)
+                value = value.repeat_interleave(hq // hk, dim=1)
+            kt, vt = key.transpose(0, 1), value.transpose(0, 1)  # [H, n, D]
+            out = torch.empty_like(query)
+            idx = torch.arange(n, device=query.device)
+            for i0 in range(0, n, _PREFILL_ROWS):
+                i1 = min(n, i0 + _PREFILL_ROWS)
+                mask = (req[i0:i1, None] == req[None, :i1]) & (idx[i0:i1, None] >= idx[None, :i1])
+                o = torch.nn.functional.scaled_dot_product_attention(
+                    query[i0:i1].transpose(0, 1), kt[:, :i1], vt[:, :i1], attn_mask=mask, scale=self.scale)
+                out[i0:i1] = o.transpose(0, 1)
+            return out
+
+        def _decode_attention(self, query, kv_cache, attn_metadata, out, n):
             """All requests of the step in one launch, output in place."""
             global _KERNEL_CALLS
-            d = self.head_size
-            out = output[:n].view(n, self.num_heads, d)
             self._slm_decode_batched(
                 query, kv_cache, attn_metadata.block_table[:n], attn_metadata.seq_lens[:n],
                 block_size=kv_cache.shape[1], num_kv_heads=kv_cache.shape[2], out=out,
-                sm_scale=1.0 / math.sqrt(d), max_seq_len=int(attn_metadata.max_seq_len))
+                sm_scale=self.scale, max_seq_len=int(attn_metadata.max_seq_len))
             _KERNEL_CALLS += 1
             if getattr(self, "_slm_logged", False) is False:
                 self._slm_logged = True
-                logger.info("slm-turbo 4-bit decode kernel serving inside vLLM (head_size=%d)", d)
+                logger.info("slm-turbo 4-bit decode kernel serving inside vLLM (head_size=%d)",
+                            self.head_size)
             return out
 
     class _Backend(TritonAttentionBackend):
@@ -225,10 +329,3 @@ def register_plugin() -> None:
     """vLLM ``general_plugins`` entry point: registers in every vLLM process."""
     _register_custom_backend()
 
-
-def _kernel_eligible_device() -> bool:
-    """True on a CUDA device the sm_100a library can run on."""
-    try:
-        return torch.cuda.is_available() and torch.cuda.get_device_capability(0) >= (10, 0)
-    except Exception:
-        return False

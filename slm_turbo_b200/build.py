@@ -21,7 +21,7 @@ INCLUDE = ROOT / "include"
 LIB_NAME = "libslm_turbo_b200.so"
 LIB_PATH = HERE / LIB_NAME
 SOURCES = ["decode.cu", "store.cu", "decode_noalloc.cu"]
-HEADERS = ["ptx.cuh", "decode_common.cuh", "decode_kernels.cuh", "internal.h"]
+HEADERS = ["ptx.cuh", "decode_common.cuh", "decode_kernels.cuh", "quant_store.cuh", "internal.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -1,6 +1,7 @@
 // decode.cu -- host launchers (C ABI) of the split-K decode kernels.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "decode_kernels.cuh"
@@ -23,10 +24,11 @@ using DecodeFn = void (*)(const DecodeParams);
 // consumers' row addresses are compile-time offsets; the contiguous layouts
 // address rows with a per-warp base and need no such specialisation.
 template <int D, int NT, int KVC, bool PK>
-DecodeFn decode_fn_kvc(int layout) {
+DecodeFn decode_fn_kvc(int layout, bool append) {
   switch (layout) {
     case LAYOUT_PAGED:
-      return decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK>;
+      return append ? decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, true>
+                    : decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, false>;
     case LAYOUT_PER_CHANNEL:
       return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL, KVC, PK>;
     default:
@@ -38,29 +40,29 @@ DecodeFn decode_fn_kvc(int layout) {
 // strides, one consumer warp per kv head) and tile packing (PK: at most 4
 // query heads per kv head, so two tiles share one n-tile).
 template <int D, int NT, bool PK>
-DecodeFn decode_fn_layout(int layout, int kvc) {
+DecodeFn decode_fn_layout(int layout, int kvc, bool append) {
   switch (kvc) {
     case 8:
-      return decode_fn_kvc<D, NT, 8, PK>(layout);
+      return decode_fn_kvc<D, NT, 8, PK>(layout, append);
     case 4:
-      return decode_fn_kvc<D, NT, 4, PK>(layout);
+      return decode_fn_kvc<D, NT, 4, PK>(layout, append);
     case 2:
-      return decode_fn_kvc<D, NT, 2, PK>(layout);
+      return decode_fn_kvc<D, NT, 2, PK>(layout, append);
     default:
-      return decode_fn_kvc<D, NT, 1, PK>(layout);
+      return decode_fn_kvc<D, NT, 1, PK>(layout, append);
   }
 }
 
 template <int D>
-DecodeFn decode_fn_d(int nt, bool pk, int layout, int kvc) {
-  if (nt == 2) return decode_fn_layout<D, 2, false>(layout, kvc);
-  return pk ? decode_fn_layout<D, 1, true>(layout, kvc) : decode_fn_layout<D, 1, false>(layout, kvc);
+DecodeFn decode_fn_d(int nt, bool pk, int layout, int kvc, bool append) {
+  if (nt == 2) return decode_fn_layout<D, 2, false>(layout, kvc, append);
+  return pk ? decode_fn_layout<D, 1, true>(layout, kvc, append) : decode_fn_layout<D, 1, false>(layout, kvc, append);
 }
 
-DecodeFn decode_fn(int D, int nt, bool pk, int layout, int kvc) {
-  if (D == 64) return decode_fn_d<64>(nt, pk, layout, kvc);
-  if (D == 80) return decode_fn_d<80>(nt, pk, layout, kvc);
-  return decode_fn_d<128>(nt, pk, layout, kvc);
+DecodeFn decode_fn(int D, int nt, bool pk, int layout, int kvc, bool append) {
+  if (D == 64) return decode_fn_d<64>(nt, pk, layout, kvc, append);
+  if (D == 80) return decode_fn_d<80>(nt, pk, layout, kvc, append);
+  return decode_fn_d<128>(nt, pk, layout, kvc, append);
 }
 
 struct OccEntry {
@@ -91,6 +93,11 @@ int occupancy(int device, const void* fn, int threads, int smem) {
 
 std::mutex g_sm_mu;
 int g_sms[64] = {0};
+
+// Process-wide knobs read at every launch (slmt_set_wait_limit_ns,
+// slmt_set_debug_stall).
+std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
+std::atomic<int> g_debug_stall{0};
 
 }  // namespace
 
@@ -181,6 +188,8 @@ int64_t workspace_floats(int64_t slots, const Geometry& g, int D) {
   return slots * (int64_t)g.kvc * g.G * (D + 2);
 }
 
+}  // namespace
+
 // Scratch layout: [segment arrival counters (int32, zero between calls)]
 // [partial rows (float) D per head] [partial (m, l) pairs].  The counter
 // region is the first workspace_bytes/64 (rounded up to 256) bytes whatever
@@ -189,6 +198,8 @@ int64_t workspace_floats(int64_t slots, const Geometry& g, int D) {
 // segment brings at least 264 bytes of partials (one head of D+2 >= 66
 // floats), so a workspace that holds a call's partials holds its counters.
 int64_t counter_region(int64_t workspace_bytes) { return (workspace_bytes / 64 + 255) / 256 * 256; }
+
+namespace {
 
 int64_t workspace_total(int64_t slots, int64_t segments, const Geometry& g, int D) {
   const int64_t pb = workspace_floats(slots, g, D) * 4;
@@ -241,7 +252,7 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.nqbuf = nqbuf;
   p.stage_offset = stage_offset;
 
-  DecodeFn fn = decode_fn(D, geo.nt, geo.pk, layout, geo.kvc);
+  DecodeFn fn = decode_fn(D, geo.nt, geo.pk, layout, geo.kvc, p.append != 0);
   const int occ = occupancy(dev, reinterpret_cast<const void*>(fn), threads, smem);
   if (occ <= 0) return SLMT_ERR_CUDA;
   const int64_t per_sm = std::min(occ, ctas_per_sm(geo.kvc, geo.nt));  // keeps the workspace bound
@@ -265,8 +276,27 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.out_dtype = out_dtype;
   p.out_seq_stride = out_seq_stride;
   p.out_head_stride = out_head_stride;
+  p.wait_limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  p.debug_stall = g_debug_stall.load(std::memory_order_relaxed);
 
-  fn<<<(unsigned)nc, threads, smem, st>>>(p);
+  // A CTA whose range ends inside a segment waits for the other CTAs that
+  // cover it, so all nc CTAs must be resident at once: a cooperative launch
+  // guarantees it (and fails up front, instead of stalling, if they cannot
+  // be).  nc never exceeds SMs x resident CTAs per SM.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)nc);
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, fn, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return SLMT_ERR_CUDA;
+  }
   return launch_status();
 }
 
@@ -400,6 +430,13 @@ extern "C" const char* slmt_status_string(int status) {
   }
 }
 
+extern "C" int64_t slmt_set_wait_limit_ns(int64_t ns) {
+  const uint64_t v = ns > 0 ? (uint64_t)ns : kDefaultWaitLimitNs;
+  return (int64_t)g_wait_limit_ns.exchange(v);
+}
+
+extern "C" int slmt_set_debug_stall(int on) { return g_debug_stall.exchange(on ? 1 : 0); }
+
 extern "C" int slmt_device_sm_count(int device) {
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
@@ -422,7 +459,13 @@ extern "C" int64_t slmt_decode_workspace_bytes(int64_t num_seqs, int64_t num_q_h
   return workspace_total(slots, segments, geo, (int)head_dim);
 }
 
-extern "C" int slmt_paged_decode(
+namespace slmt {
+namespace {
+
+// Shared by slmt_paged_decode and slmt_paged_append_decode (append != 0: one
+// new token per sequence, quantized into the cache at position len-1 by the
+// decode launch itself).
+int paged_decode_impl(
     const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
     const uint8_t* kv_cache, int64_t num_blocks, int64_t block_size,
     int64_t num_kv_heads, int64_t head_dim, const void* block_tables,
@@ -430,7 +473,8 @@ extern "C" int slmt_paged_decode(
     const int32_t* seq_lens, int64_t seq_len_scalar, int64_t max_seq_len_hint,
     int64_t num_seqs, int64_t num_q_heads, float sm_scale, void* out,
     int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
-    void* workspace, int64_t workspace_bytes, int32_t* err_flag, void* stream) {
+    void* workspace, int64_t workspace_bytes, int32_t* err_flag, void* stream,
+    const void* new_key, const void* new_value, int kv_dtype, int64_t new_seq_stride) {
   if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
   if (num_seqs < 0 || num_blocks < 0 || block_size <= 0 || max_blocks_per_seq < 0)
     return SLMT_ERR_SHAPE;
@@ -467,6 +511,18 @@ extern "C" int slmt_paged_decode(
     p.paged_mode = 1;
   else
     p.paged_mode = 2;
+  if (new_key || new_value) {
+    if (!new_key || !new_value || !seq_lens) return SLMT_ERR_NULL;
+    if (kv_dtype != SLMT_DTYPE_F16 && kv_dtype != SLMT_DTYPE_BF16) return SLMT_ERR_DTYPE;
+    if (new_seq_stride < num_kv_heads * head_dim) return SLMT_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(new_key) | reinterpret_cast<uintptr_t>(new_value)) % 2 != 0)
+      return SLMT_ERR_ALIGN;
+    p.append = 1;
+    p.new_bf16 = kv_dtype == SLMT_DTYPE_BF16;
+    p.new_k = new_key;
+    p.new_v = new_value;
+    p.new_seq_stride = new_seq_stride;
+  }
   p.seq_lens = seq_lens;
   p.seq_len_scalar = (int)seq_len_scalar;
   p.causal_rows = 0;
@@ -481,6 +537,43 @@ extern "C" int slmt_paged_decode(
   return launch_decode(p, LAYOUT_PAGED, (int)head_dim, geo, chunks_upper, workspace,
                        workspace_bytes, out, out_dtype_code(out_dtype), out_seq_stride,
                        out_head_stride, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+}  // namespace slmt
+
+extern "C" int slmt_paged_decode(
+    const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+    const uint8_t* kv_cache, int64_t num_blocks, int64_t block_size,
+    int64_t num_kv_heads, int64_t head_dim, const void* block_tables,
+    int bt_dtype, int64_t bt_seq_stride, int64_t max_blocks_per_seq,
+    const int32_t* seq_lens, int64_t seq_len_scalar, int64_t max_seq_len_hint,
+    int64_t num_seqs, int64_t num_q_heads, float sm_scale, void* out,
+    int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
+    void* workspace, int64_t workspace_bytes, int32_t* err_flag, void* stream) {
+  return paged_decode_impl(q, q_dtype, q_seq_stride, q_head_stride, kv_cache, num_blocks, block_size,
+                           num_kv_heads, head_dim, block_tables, bt_dtype, bt_seq_stride, max_blocks_per_seq,
+                           seq_lens, seq_len_scalar, max_seq_len_hint, num_seqs, num_q_heads, sm_scale, out,
+                           out_dtype, out_seq_stride, out_head_stride, workspace, workspace_bytes, err_flag,
+                           stream, nullptr, nullptr, SLMT_DTYPE_F16, 0);
+}
+
+extern "C" int slmt_paged_append_decode(
+    const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+    const void* new_key, const void* new_value, int kv_dtype, int64_t new_seq_stride,
+    uint8_t* kv_cache, int64_t num_blocks, int64_t block_size,
+    int64_t num_kv_heads, int64_t head_dim, const void* block_tables,
+    int bt_dtype, int64_t bt_seq_stride, int64_t max_blocks_per_seq,
+    const int32_t* seq_lens, int64_t max_seq_len_hint, int64_t num_seqs,
+    int64_t num_q_heads, float sm_scale, void* out, int out_dtype,
+    int64_t out_seq_stride, int64_t out_head_stride, void* workspace,
+    int64_t workspace_bytes, int32_t* err_flag, void* stream) {
+  if (!new_key || !new_value || !seq_lens) return SLMT_ERR_NULL;
+  return paged_decode_impl(q, q_dtype, q_seq_stride, q_head_stride, kv_cache, num_blocks, block_size,
+                           num_kv_heads, head_dim, block_tables, bt_dtype, bt_seq_stride, max_blocks_per_seq,
+                           seq_lens, 0, max_seq_len_hint, num_seqs, num_q_heads, sm_scale, out, out_dtype,
+                           out_seq_stride, out_head_stride, workspace, workspace_bytes, err_flag, stream,
+                           new_key, new_value, kv_dtype, new_seq_stride);
 }
 
 extern "C" int slmt_per_channel_decode(

@@ -16,7 +16,7 @@ __host__ __device__ constexpr int ctas_per_sm(int kvc, int nt) {
 constexpr int kMaxStages = 8;
 constexpr int kTileTokens = 16;   // one m16 tensor-core tile of tokens
 constexpr int kChunkTokens = 32;  // one pipeline stage = two tiles
-constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s per wait
+constexpr uint64_t kDefaultWaitLimitNs = 4000000000ull;  // 4 s per wait (host-settable)
 constexpr uint64_t kDrainLimitNs = 200000000ull;  // 0.2 s per drain wait
 constexpr float kRescaleSlack = 4.0f;  // lazy softmax rescale threshold (log2 units)
 constexpr float kMaxFloor = -1e30f;    // running max before any score (finite on purpose)
@@ -38,7 +38,8 @@ struct ChunkDesc {
   int ncov;       // CTAs whose chunk ranges cover this segment
   int c_first;    // first of them
   int nmergers;   // how many of them end their range inside it (they merge it)
-  int pad[3];
+  int len;        // the sequence's length
+  int pad[2];
 };
 
 // Descriptor flag bits.
@@ -46,6 +47,8 @@ constexpr int kFlagFirst = 1;     // first chunk of the segment in this CTA
 constexpr int kFlagLast = 2;      // last chunk of the segment in this CTA
 constexpr int kFlagQbuf = 4;      // q buffer index (0/1)
 constexpr int kFlagRangeEnd = 8;  // last chunk of this CTA's range
+constexpr int kFlagSegEnd = 16;   // final chunk of the segment (holds its newest token)
+constexpr int kFlagOwnsEnd = 32;  // with kFlagFirst: this CTA's range holds the final chunk
 
 // The split segment this CTA helps merge after its main loop: the segment
 // its range ends in.  Every CTA whose range ends inside a split segment
@@ -60,15 +63,24 @@ struct SmemHeader {
   uint64_t empty[kMaxStages];
   uint64_t qfull[2];
   uint64_t qempty[2];
+  uint64_t never;  // a barrier nothing arrives on (the stalled-consumer test hook)
+  // fused append: the new token's slot per consumer warp (kv head), quantized
+  // at the segment's start in this CTA and copied over the stale staged row
+  // when the segment's final chunk arrives
+  uint8_t newslot[8][136];
+  uint64_t prologue;  // fused append: the producer published its first segment
+  int pro_seq, pro_kg, pro_len;  // that segment if its final chunk is in range (pro_seq -1: none)
   ChunkDesc desc[kMaxStages];
   int has_job;
   int merge_ok;
+  int abort;  // a consumer warp gave up on a wait: the others skip the merge
   MergeJob job;
 };
 
 // Per-segment word in the scratch's counter region: low 16 bits count the
-// CTAs that published a partial, high 16 bits the mergers that are done;
-// the last merger resets the word to zero.
+// consumer warps that published their slice of a partial (KVC per covering
+// CTA), high 16 bits the mergers that are done; the last merger resets the
+// word to zero.
 constexpr uint32_t kArriveOne = 1u, kDoneOne = 1u << 16;
 
 constexpr int kHeaderBytes = (int)((sizeof(SmemHeader) + 127) / 128 * 128);
@@ -117,6 +129,15 @@ struct DecodeParams {
   float* part_acc;     // [slots][kvc*G][D]  (unnormalised output)
   int32_t* seg_count;  // [ngroups*B] arrivals per segment; zero between launches
   int32_t* err;
+  // fused append (paged layout): one new token per sequence at position
+  // len-1, row (seq, kv head) at new_k/new_v + seq*new_seq_stride + head*D,
+  // quantized into the cache by the warp that consumes the segment's final chunk
+  int append, new_bf16;
+  const void* new_k;
+  const void* new_v;
+  int64_t new_seq_stride;
+  uint64_t wait_limit_ns;  // bound of every pipeline / merge wait
+  int debug_stall;         // test hook: CTA 0's consumers wait on a flag nothing sets
   // output element (seq, head, d) at out + seq*out_seq_stride + head*out_head_stride + d
   void* out;
   int out_dtype;  // 0 f16, 1 bf16, 2 f32

@@ -33,6 +33,7 @@
 
 #include "decode_common.cuh"
 #include "ptx.cuh"
+#include "quant_store.cuh"
 
 namespace slmt {
 
@@ -221,7 +222,7 @@ __device__ __forceinline__ bool next_segment(const DecodeParams& p, int s, int k
   return true;
 }
 
-template <int D, int LAYOUT>
+template <int D, int LAYOUT, bool APPEND>
 __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
                                 uint8_t* qbuf, uint8_t* rbuf, uint8_t* stg) {
   constexpr int SLOT = D + 8;
@@ -260,6 +261,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
   }
 
   const uint64_t policy = l2_evict_first_policy();
+  uint32_t q_issued[2] = {0u, 0u};  // q (+ ruler) copies issued per q buffer
   uint32_t it = 0;
   int stage = 0;
   uint32_t phase = 0;
@@ -288,6 +290,17 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     int chunk = (int)(tt - ps);
     int L = seq_len_of(p, s);
     int nch = nchunks_of(L);
+    if constexpr (APPEND) {
+      // publish the range's first segment: its consumers quantize its new
+      // token now, while the first copies are in flight, if this range holds
+      // the segment's final chunk
+      if (lane == 0) {
+        hdr->pro_seq = (t_begin - chunk + nch - 1 < t_end) ? s : -1;
+        hdr->pro_kg = kg;
+        hdr->pro_len = L;
+        mbar_arrive(&hdr->prologue);
+      }
+    }
     bool first = true;
     uint32_t seg = 0;  // segments started by this CTA
     int seg_ncov = 1, seg_cfirst = c, seg_mergers = 0;
@@ -313,7 +326,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
 
     for (long long t = t_begin; t < t_end; ++t) {
       if (it >= (uint32_t)p.stages) {
-        if (!mbar_wait(&hdr->empty[stage], phase ^ 1u, kWaitLimitNs)) {
+        if (!mbar_wait(&hdr->empty[stage], phase ^ 1u, p.wait_limit_ns)) {
           failed = true;
           break;
         }
@@ -331,8 +344,13 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       }
       const bool last = (chunk == nch - 1) || (t == t_end - 1);
       const int nvalid = min(kChunkTokens, L - chunk * kChunkTokens);
-      const int flags = (first ? kFlagFirst : 0) | (last ? kFlagLast : 0) | (qb ? kFlagQbuf : 0) |
-                        (t == t_end - 1 ? kFlagRangeEnd : 0);
+      int flags = (first ? kFlagFirst : 0) | (last ? kFlagLast : 0) | (qb ? kFlagQbuf : 0) |
+                  (t == t_end - 1 ? kFlagRangeEnd : 0);
+      bool owns_end = false;
+      if constexpr (APPEND) {
+        owns_end = first && (t - chunk + nch - 1 < t_end);
+        flags |= (chunk == nch - 1 ? kFlagSegEnd : 0) | (owns_end ? kFlagOwnsEnd : 0);
+      }
       const int slot = (int)(c + (int64_t)kg * B + s);
       uint8_t* dst = stg + (size_t)stage * p.stage_bytes;
       uint64_t* fb = &hdr->full[stage];
@@ -359,7 +377,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           const uint32_t tile_bytes = (uint32_t)(kTileTokens * row_bytes);
           const uint32_t tx = (ok0 ? tile_bytes : 0u) + (ok1 ? tile_bytes : 0u);
           if (lane == 0) {
-            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, {0, 0, 0}};
+            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, APPEND ? L : 0, {0, 0}};
           }
           __syncwarp();
           if (lane == 0) {
@@ -386,7 +404,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           }
           const unsigned okm = __ballot_sync(0xffffffffu, ok);
           if (lane == 0) {
-            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, {0, 0, 0}};
+            hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, APPEND ? L : 0, {0, 0}};
           }
           const uint8_t* src =
               p.cache + ((phys * bs + (tok % bs)) * p.kv_total + (int64_t)kg * p.kvc) * SLOT;
@@ -424,7 +442,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           }
         }
         if (lane == 0) {
-          hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, {0, 0, 0}};
+          hdr->desc[stage] = ChunkDesc{s, kg, chunk, nvalid, flags, slot, seg_ncov, seg_cfirst, seg_mergers, APPEND ? L : 0, {0, 0}};
         }
         // stage: K block [kvc][32 rows][D/2] then V block of the same shape
         const int kblock = p.kvc * kChunkTokens * HALF;
@@ -464,12 +482,22 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       }
       cp_async_arrive_noinc(fb);
 
+      if (APPEND && owns_end) {
+        // the consumers quantize the group's new K/V rows when this segment
+        // starts: pull them into L2 now (one 128-byte line per lane)
+        const int64_t row0 = (int64_t)s * p.new_seq_stride + (int64_t)kg * p.kvc * D;
+        const int lines = (p.kvc * D * 2 + 127) / 128;
+        for (int i = lane; i < 2 * lines; i += 32) {
+          const void* base = (i < lines) ? p.new_k : p.new_v;
+          prefetch_l2(reinterpret_cast<const uint8_t*>(base) + row0 * 2 + (int64_t)(i % lines) * 128);
+        }
+      }
       if (first) {
         // ---- q (raw fp16/bf16) and per-channel rulers of this segment, staged
         // after the segment's first chunk is already in flight ----
         const uint32_t use = seg / (uint32_t)p.nqbuf;
         if (use >= 1) {
-          if (!mbar_wait(&hdr->qempty[qb], (use - 1) & 1u, kWaitLimitNs)) {
+          if (!mbar_wait(&hdr->qempty[qb], (use - 1) & 1u, p.wait_limit_ns)) {
             failed = true;
             ++it;
             break;
@@ -502,6 +530,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           }
         }
         __syncwarp();
+        ++q_issued[qb];
         if (lane == 0) {
           mbar_arrive_expect_tx(&hdr->qfull[qb], qtx + rtx);
           if (qtx) bulk_g2s(qd, qsrc, qtx, &hdr->qfull[qb], policy);
@@ -549,21 +578,30 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     }
   }
 
+  if constexpr (APPEND) {
+    if (t_begin >= t_end && lane == 0) {  // empty range: nothing to publish
+      hdr->pro_seq = -1;
+      mbar_arrive(&hdr->prologue);
+    }
+  }
   if (!failed) {
     // terminal descriptor
     if (it >= (uint32_t)p.stages) {
-      if (!mbar_wait(&hdr->empty[stage], phase ^ 1u, kWaitLimitNs)) failed = true;
+      if (!mbar_wait(&hdr->empty[stage], phase ^ 1u, p.wait_limit_ns)) failed = true;
     }
     if (!failed) {
       if (lane == 0) hdr->desc[stage].seq = -1;
       __syncwarp();
       if (lane == 0) mbar_arrive(&hdr->full[stage]);
       cp_async_arrive_noinc(&hdr->full[stage]);
-      return;
+      ++it;
     }
   }
-  // failure: flag it and wait (bounded) for the copies this warp issued
-  if (lane == 0) set_err(p, 4u);
+  if (failed && lane == 0) set_err(p, 4u);
+  // Wait (bounded) until every copy this warp issued has landed, so that the
+  // CTA never exits with a copy into its shared memory in flight -- also
+  // when the consumers gave up early.  Stages the consumers already waited
+  // for pass at once.
   const uint32_t n = it < (uint32_t)p.stages ? it : (uint32_t)p.stages;
   for (uint32_t k = 0; k < n; ++k) {
     const uint32_t i = it - 1 - k;
@@ -571,6 +609,8 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     const uint32_t ph = (i / (uint32_t)p.stages) & 1u;
     mbar_wait(&hdr->full[st], ph, kDrainLimitNs);
   }
+  for (int b = 0; b < 2; ++b)
+    if (q_issued[b]) mbar_wait(&hdr->qfull[b], (q_issued[b] - 1u) & 1u, kDrainLimitNs);
 }
 
 // Output element store in the requested dtype (0 f16, 1 bf16, 2 f32).
@@ -584,6 +624,9 @@ __device__ __forceinline__ void store_out(const DecodeParams& p, int64_t off, fl
 }
 
 // Barrier of the CTA's consumer threads only (the producer warp never joins).
+// Every consumer warp reaches each of these the same number of times: a warp
+// that gives up on a wait leaves the main loop for the barrier after it (it
+// never returns early), so no warp is left waiting here.
 template <int NCW>
 __device__ __forceinline__ void consumer_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
@@ -978,7 +1021,30 @@ __device__ __forceinline__ void fold_v_bias(WarpState<D, NT>& w) {
   }
 }
 
-template <int D, int NT, int LAYOUT, int KVC, bool PK>
+// Fused append (paged layout): kv head h's new row of sequence `seq` (its
+// newest token, position t = len-1) is quantized by this warp with the store
+// kernel's arithmetic; the slot goes to the cache (for later launches) and to
+// hdr->newslot[j], which replaces the stale staged copy of the slot when the
+// segment's final chunk arrives.
+template <int D, int KVC>
+__device__ __forceinline__ void append_token(const DecodeParams& p, SmemHeader* hdr, int seq, int h, int t,
+                                             int j) {
+  const int lane = threadIdx.x & 31;
+  const int64_t ph = block_entry(p, seq, t / p.block_size);
+  const int64_t off = ((int64_t)seq * p.new_seq_stride + (int64_t)h * D) * 2;  // bytes
+  const SlotRow nr = quantize_slot_row<D>(reinterpret_cast<const uint8_t*>(p.new_k) + off,
+                                          reinterpret_cast<const uint8_t*>(p.new_v) + off, p.new_bf16);
+  if (ph >= 0 && ph < p.num_blocks)
+    write_slot_row<D>(const_cast<uint8_t*>(p.cache) +
+                          ((ph * p.block_size + t % p.block_size) * p.kv_total + h) * (int64_t)(D + 8),
+                      nr);
+  else if (lane == 0)
+    set_err(p, 1u);
+  write_slot_row<D>(hdr->newslot[j], nr);
+  __syncwarp();
+}
+
+template <int D, int NT, int LAYOUT, int KVC, bool PK, bool APPEND>
 __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
                                 const uint8_t* qbuf, const uint8_t* rbuf,
                                 const uint8_t* stg) {
@@ -994,11 +1060,43 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
   WarpState<D, NT> w;
   int stage = 0;
   uint32_t phase = 0, seg = 0;
+  // A failed wait sets the error bit and the abort flag and leaves the loop
+  // for the barrier after it.
+  auto give_up = [&]() {
+    if (lane == 0) {
+      set_err(p, 4u);
+      hdr->abort = 1;
+    }
+  };
 
-  while (true) {
-    if (!mbar_wait(&hdr->full[stage], phase, kWaitLimitNs)) {
-      if (lane == 0) set_err(p, 4u);
-      return;
+  bool run = true;
+  bool pre_done = false;  // the range's first segment's new token is quantized
+  if (p.debug_stall && blockIdx.x == 0) {
+    // Test hook (off unless the host sets it): CTA 0's consumer warps wait
+    // for a barrier phase that nothing completes, so the wait runs out after
+    // p.wait_limit_ns; the producer then times out on the ring and drains.
+    if (!mbar_wait(&hdr->never, 0u, p.wait_limit_ns)) give_up();
+    run = false;
+  }
+
+  if constexpr (APPEND) {
+    // Fused append, first segment of the range: quantize its new token while
+    // the producer's first copies are in flight.
+    if (run) {
+      if (!mbar_wait(&hdr->prologue, 0u, p.wait_limit_ns)) {
+        give_up();
+        run = false;
+      } else if (hdr->pro_seq >= 0) {
+        append_token<D, KVC>(p, hdr, hdr->pro_seq, hdr->pro_kg * kvc + j, hdr->pro_len - 1, j);
+        pre_done = true;
+      }
+    }
+  }
+
+  while (run) {
+    if (!mbar_wait(&hdr->full[stage], phase, p.wait_limit_ns)) {
+      give_up();
+      break;
     }
     const ChunkDesc& dsm = hdr->desc[stage];
     if (dsm.seq < 0) break;
@@ -1006,11 +1104,21 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
     const int flags = dsm.flags, slot = dsm.slot, nvalid = dsm.nvalid;
     const int qbi = (flags & kFlagQbuf) ? 1 : 0;
 
+    if constexpr (APPEND) {
+      if ((flags & kFlagFirst) && (flags & kFlagOwnsEnd)) {
+        // a later segment whose final chunk this CTA decodes: quantize its
+        // new token now (no softmax state is live at a segment start)
+        if (pre_done)
+          pre_done = false;  // the range's first segment: done at the start
+        else
+          append_token<D, KVC>(p, hdr, dsm.seq, dsm.kg * kvc + j, dsm.len - 1, j);
+      }
+    }
     if (flags & kFlagFirst) {
       // ---- segment start: q fragments, q sums, fresh softmax state ----
-      if (!mbar_wait(&hdr->qfull[qbi], (seg / (uint32_t)p.nqbuf) & 1u, kWaitLimitNs)) {
-        if (lane == 0) set_err(p, 4u);
-        return;
+      if (!mbar_wait(&hdr->qfull[qbi], (seg / (uint32_t)p.nqbuf) & 1u, p.wait_limit_ns)) {
+        give_up();
+        break;
       }
       const __half* qh = reinterpret_cast<const __half*>(qbuf + qbi * p.qbuf_bytes) + (size_t)j * G * D;
       const __half* ksc = reinterpret_cast<const __half*>(rbuf + qbi * p.rbuf_bytes) + (size_t)j * D;
@@ -1084,6 +1192,18 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 
     {
       const uint8_t* st = stg + (size_t)stage * p.stage_bytes;
+      if constexpr (APPEND) {
+        if (flags & kFlagSegEnd) {
+          // the segment's newest token is the last valid row of this chunk:
+          // its slot, quantized at the segment start, replaces the staged copy
+          // (read from the cache before this launch wrote it)
+          uint8_t* row = const_cast<uint8_t*>(st) + (nvalid - 1) * StageView<D, LAYOUT, KVC>::kRow + j * (D + 8);
+          if (lane < (D + 8) / 8)
+            reinterpret_cast<uint2*>(row)[lane] = reinterpret_cast<const uint2*>(hdr->newslot[j])[lane];
+          fence_proxy_async_shared();  // before the producer's next copy reuses the stage
+          __syncwarp();
+        }
+      }
       StageView<D, LAYOUT, KVC> sv;
       if (LAYOUT == LAYOUT_PAGED) {
         sv.base = st + j * (D + 8);
@@ -1178,16 +1298,15 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
         }
       }
       if (!direct) {
-        // publish the partial; if this CTA's range ends in the segment it
-        // merges a slice of it after its main loop
+        // publish this warp's slice of the partial (each consumer warp counts
+        // itself); if this CTA's range ends in the segment it merges a slice
+        // of it after its main loop
         __threadfence();
-        consumer_bar<KVC>();
-        if (threadIdx.x == 0) {
-          atomicAdd(reinterpret_cast<unsigned int*>(p.seg_count) + e_seg, kArriveOne);
-          if (flags & kFlagRangeEnd) {
-            hdr->job = MergeJob{e_seg, seq, kgrp, c_first, ncov, dd.nmergers};
-            hdr->has_job = 1;
-          }
+        __syncwarp();
+        if (lane == 0) atomicAdd(reinterpret_cast<unsigned int*>(p.seg_count) + e_seg, kArriveOne);
+        if (threadIdx.x == 0 && (flags & kFlagRangeEnd)) {
+          hdr->job = MergeJob{e_seg, seq, kgrp, c_first, ncov, dd.nmergers};
+          hdr->has_job = 1;
         }
       }
       if (LAYOUT == LAYOUT_PER_CHANNEL) {
@@ -1210,13 +1329,15 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
   // ---- this CTA's slice of the merge of the split segment its range ends
   // in (the stage ring is idle now: every copy has landed and been consumed) ----
   consumer_bar<KVC>();
+  if (hdr->abort) return;  // every consumer warp returns here together
   if (hdr->has_job) {
     const MergeJob job = hdr->job;
     unsigned int* word = reinterpret_cast<unsigned int*>(p.seg_count) + job.e_seg;
     if (threadIdx.x == 0) {
-      // every covering CTA publishes before it waits on anything, so this
-      // wait ends; it is bounded all the same
-      const bool ok = spin_until_arrived(word, (unsigned)job.ncov, kWaitLimitNs);
+      // every covering CTA publishes before it waits on anything, and a
+      // cooperative launch makes all of them resident, so this wait ends;
+      // it is bounded all the same
+      const bool ok = spin_until_arrived(word, (unsigned)(job.ncov * KVC), p.wait_limit_ns);
       if (!ok) set_err(p, 4u);
       hdr->merge_ok = ok ? 1 : 0;
     }
@@ -1243,9 +1364,13 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 // CTAs per SM are chosen for about 18 warps per SM with one n-tile (96
 // registers: a sub-partition holds up to 5 warps of its 16K registers) and
 // about 9 with two n-tiles.
-template <int D, int NT, int LAYOUT, int KVC, bool PK>
+// APPEND (paged layout only): the launch also quantizes each sequence's new
+// token into the cache (slmt_paged_append_decode); a separate instantiation,
+// so the plain decode carries none of that code.
+template <int D, int NT, int LAYOUT, int KVC, bool PK, bool APPEND = false>
 __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
     decode_splitk_kernel(const __grid_constant__ DecodeParams p) {
+  static_assert(!APPEND || LAYOUT == LAYOUT_PAGED, "the fused append writes the paged layout");
   extern __shared__ __align__(128) uint8_t smem[];
   SmemHeader* hdr = reinterpret_cast<SmemHeader*>(smem);
   uint8_t* qbuf = smem + kHeaderBytes;
@@ -1260,14 +1385,17 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
       mbar_init(&hdr->qfull[i], 1);
       mbar_init(&hdr->qempty[i], KVC);
     }
+    mbar_init(&hdr->never, 1);
+    mbar_init(&hdr->prologue, 1);
     hdr->has_job = 0;
+    hdr->abort = 0;
     fence_mbar_init();
   }
   __syncthreads();
   if (threadIdx.x >= KVC * 32)
-    decode_producer<D, LAYOUT>(p, hdr, qbuf, rbuf, stg);
+    decode_producer<D, LAYOUT, APPEND>(p, hdr, qbuf, rbuf, stg);
   else
-    decode_consumer<D, NT, LAYOUT, KVC, PK>(p, hdr, qbuf, rbuf, stg);
+    decode_consumer<D, NT, LAYOUT, KVC, PK, APPEND>(p, hdr, qbuf, rbuf, stg);
 }
 
 }  // namespace slmt

@@ -16,6 +16,7 @@
 
 #include <mutex>
 
+#include "internal.h"
 #include "slm_turbo_b200.h"
 
 namespace {
@@ -31,7 +32,9 @@ void* g_scratch[kMaxDevices] = {};
 
 // Device address of g_decode_scratch in the context of device `dev` (the
 // current device).  The lookup runs once per device, on the first call made
-// there, and is cached.
+// there, and is cached for the life of the process: the cache assumes the
+// device's primary context lives that long (after cudaDeviceReset the module
+// is loaded again elsewhere and the cached address is stale).
 int scratch_address(int dev, void** out) {
   if (dev >= 0 && dev < kMaxDevices) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -72,8 +75,8 @@ extern "C" int slmt_paged_decode_noalloc(
   if (rc != SLMT_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (reset_scratch) {
-    // The counters occupy the first 1/64 of the array (rounded up to 256 bytes).
-    const size_t zero = ((size_t)SLMT_NOALLOC_SCRATCH_BYTES / 64 + 255) / 256 * 256;
+    // the counter region of a workspace of the array's size
+    const size_t zero = (size_t)slmt::counter_region((int64_t)SLMT_NOALLOC_SCRATCH_BYTES);
     if (cudaMemsetAsync(scratch, 0, zero, st) != cudaSuccess) return SLMT_ERR_CUDA;
   }
   return slmt_paged_decode(q, q_dtype, q_seq_stride, q_head_stride, kv_cache, num_blocks, block_size,

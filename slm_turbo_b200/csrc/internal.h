@@ -21,4 +21,9 @@ inline int launch_status() {
 // SM count of the current device, cached per device id.
 int current_device_sms(int* device_out);
 
+// Bytes at the start of a split-K workspace of `workspace_bytes` that hold
+// the per-segment arrival counters (zero between calls).  Every entry point
+// that lays out or resets a workspace uses this one definition.
+int64_t counter_region(int64_t workspace_bytes);
+
 }  // namespace slmt

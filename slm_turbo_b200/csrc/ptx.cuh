@@ -102,6 +102,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0,
       : "memory");
 }
 
+// Order this thread's earlier generic-proxy accesses to shared memory before
+// later async-proxy (TMA) accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Pull the 128-byte line holding `p` into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // L2 policy for data streamed once (the packed cache).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t p;

@@ -1,8 +1,9 @@
 // store.cu -- quantize-on-write kernels (sm_100a).
 //
 //  * kv_store_kernel: vLLM paged per-token layout.  One warp per (token, kv
-//    head): lanes hold 2-4 dims, warp-shuffle min/max, fp32 IEEE step and
-//    codes exactly as the reference kernel computes them
+//    head) through quantize_slot_row / write_slot_row (quant_store.cuh):
+//    lanes hold 2-4 dims, warp-shuffle min/max, fp32 IEEE step and codes
+//    exactly as the reference kernel computes them
 //    (kernels/kv_dequant_kernels.cuh:838-918), then each lane stores its
 //    packed bytes and lane 0 the four fp16 rulers with one 8-byte store.
 //  * pc_rulers_kernel / pc_codes_kernel: the per-channel quantizer of
@@ -13,6 +14,7 @@
 
 #include "internal.h"
 #include "ptx.cuh"
+#include "quant_store.cuh"
 
 namespace slmt {
 
@@ -22,8 +24,6 @@ __global__ void __launch_bounds__(128) kv_store_kernel(
     int64_t tok_stride, int num_tokens, int kv, uint8_t* __restrict__ cache,
     int64_t num_slots, const int64_t* __restrict__ slot_mapping,
     int32_t* err) {
-  constexpr int VEC = (D == 64) ? 2 : 4;  // dims per lane
-  constexpr int LANES = D / VEC;          // active lanes (32, 32, 20)
   constexpr int SLOT = D + 8;
   const int lane = threadIdx.x & 31;
   const int64_t wid = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -36,81 +36,10 @@ __global__ void __launch_bounds__(128) kv_store_kernel(
     return;
   }
   const int64_t row = (int64_t)tok * tok_stride + (int64_t)kvh * D;
-  const bool act = lane < LANES;
-  float xk[VEC], xv[VEC];
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    xk[i] = 0.f;
-    xv[i] = 0.f;
-  }
-  if (act) {
-    if (in_bf16) {
-      const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(key) + row + lane * VEC;
-      const __nv_bfloat16* vp = reinterpret_cast<const __nv_bfloat16*>(value) + row + lane * VEC;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        xk[i] = __bfloat162float(kp[i]);
-        xv[i] = __bfloat162float(vp[i]);
-      }
-    } else {
-      const __half* kp = reinterpret_cast<const __half*>(key) + row + lane * VEC;
-      const __half* vp = reinterpret_cast<const __half*>(value) + row + lane * VEC;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        xk[i] = __half2float(kp[i]);
-        xv[i] = __half2float(vp[i]);
-      }
-    }
-  }
-  float kmn = INFINITY, kmx = -INFINITY, vmn = INFINITY, vmx = -INFINITY;
-  if (act) {
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      kmn = fminf(kmn, xk[i]);
-      kmx = fmaxf(kmx, xk[i]);
-      vmn = fminf(vmn, xv[i]);
-      vmx = fmaxf(vmx, xv[i]);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    kmn = fminf(kmn, __shfl_xor_sync(0xffffffffu, kmn, o));
-    kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
-    vmn = fminf(vmn, __shfl_xor_sync(0xffffffffu, vmn, o));
-    vmx = fmaxf(vmx, __shfl_xor_sync(0xffffffffu, vmx, o));
-  }
-  float kst = __fdiv_rn(kmx - kmn, 15.0f);
-  if (!(kst > 0.0f)) kst = 1.0f;  // constant row guard (ref .cuh:854)
-  float vst = __fdiv_rn(vmx - vmn, 15.0f);
-  if (!(vst > 0.0f)) vst = 1.0f;
-
-  uint8_t* base = cache + (slot * kv + kvh) * (int64_t)SLOT;
-  if (act) {
-    uint32_t kc = 0, vc = 0;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      int qk = (int)__fadd_rn(__fdiv_rn(__fsub_rn(xk[i], kmn), kst), 0.5f);
-      int qv = (int)__fadd_rn(__fdiv_rn(__fsub_rn(xv[i], vmn), vst), 0.5f);
-      qk = qk < 0 ? 0 : (qk > 15 ? 15 : qk);
-      qv = qv < 0 ? 0 : (qv > 15 ? 15 : qv);
-      kc |= (uint32_t)qk << (4 * i);
-      vc |= (uint32_t)qv << (4 * i);
-    }
-    if (VEC == 4) {
-      reinterpret_cast<uint16_t*>(base)[lane] = (uint16_t)kc;
-      reinterpret_cast<uint16_t*>(base + D / 2)[lane] = (uint16_t)vc;
-    } else {
-      base[lane] = (uint8_t)kc;
-      base[D / 2 + lane] = (uint8_t)vc;
-    }
-  }
-  if (lane == 0) {
-    const uint32_t w0 = (uint32_t)__half_as_ushort(__float2half_rn(kmn)) |
-                        ((uint32_t)__half_as_ushort(__float2half_rn(kst)) << 16);
-    const uint32_t w1 = (uint32_t)__half_as_ushort(__float2half_rn(vmn)) |
-                        ((uint32_t)__half_as_ushort(__float2half_rn(vst)) << 16);
-    *reinterpret_cast<uint2*>(base + D) = make_uint2(w0, w1);
-  }
+  const size_t esz = in_bf16 ? sizeof(__nv_bfloat16) : sizeof(__half);
+  const SlotRow r = quantize_slot_row<D>(reinterpret_cast<const uint8_t*>(key) + row * esz,
+                                         reinterpret_cast<const uint8_t*>(value) + row * esz, in_bf16);
+  write_slot_row<D>(cache + (slot * kv + kvh) * (int64_t)SLOT, r);
 }
 
 // fp16 tensor arithmetic as torch evaluates it: fp32 op, round to fp16.

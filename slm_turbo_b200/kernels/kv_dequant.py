@@ -12,6 +12,8 @@ launches go to the caller's current CUDA stream.
 
 Extensions beyond the reference (new names, nothing removed):
 ``kv_decode_paged_batched`` (the whole ragged batch in one launch),
+``kv_append_decode_paged_batched`` (a decode step's store + decode as one
+launch),
 ``kv_dequant_decode_attention_batched`` (per-channel layout with a batch
 dimension), ``kv_quantize_per_channel`` / ``kv_append_per_channel`` (the
 per-channel quantizer of kernels/benchmark/benchmark.py on the device), and
@@ -32,6 +34,7 @@ __all__ = [
     "kv_quantize_store",
     "kv_dequant_decode_per_token_paged_attention",
     "kv_decode_paged_batched",
+    "kv_append_decode_paged_batched",
     "kv_dequant_decode_attention_batched",
     "kv_quantize_per_channel",
     "kv_append_per_channel",
@@ -315,6 +318,56 @@ def kv_decode_paged_batched(q, kv_cache, block_tables, seq_lens, block_size=None
         sl = sl.to(torch.int32).contiguous()
     _paged_call(q, kv_cache, block_tables, sl, 0, bs, kv, out, sm_scale=sm_scale,
                 max_seq_len=max_seq_len)
+    return out
+
+
+def kv_append_decode_paged_batched(q, new_key, new_value, kv_cache, block_tables, seq_lens, block_size=None,
+                                   num_kv_heads=None, out=None, sm_scale=None, max_seq_len=None):
+    """One decode step in one launch: quantize each sequence's new token into
+    the cache at position seq_lens[b]-1, then decode every sequence.
+
+    q [B, Hq, D]; new_key/new_value [B, KV, D] (fp16/bf16, head rows
+    contiguous); kv_cache [NB, bs, KV, D+8] uint8 (written in place);
+    block_tables [B, max_blocks] int32/int64; seq_lens [B] int32 on the
+    device, the lengths AFTER the append.  Same result as
+    ``kv_quantize_store`` of the new tokens at their slots followed by
+    ``kv_decode_paged_batched``.  Returns out [B, Hq, D].
+    """
+    L = _lib.load()
+    B, H, D = q.shape
+    bs = kv_cache.size(1) if block_size is None else int(block_size)
+    kv = kv_cache.size(2) if num_kv_heads is None else int(num_kv_heads)
+    _require_cuda(new_key, "append-decode: new_key", _QDT)
+    if new_value.dtype != new_key.dtype:
+        raise RuntimeError("append-decode: new_key/new_value dtypes differ")
+    if tuple(new_key.shape) != (B, kv, D) or tuple(new_value.shape) != (B, kv, D):
+        raise RuntimeError(f"append-decode: new K/V must be [{B}, {kv}, {D}]")
+    if new_key.stride(2) != 1 or new_key.stride(1) != D:
+        new_key = new_key.contiguous()
+    if new_value.stride() != new_key.stride():
+        new_key, new_value = new_key.contiguous(), new_value.contiguous()
+    if kv_cache.dtype != torch.uint8 or not kv_cache.is_contiguous():
+        raise RuntimeError("append-decode: kv_cache must be contiguous uint8")
+    if out is None:
+        out = torch.empty(B, H, D, dtype=torch.float32, device=q.device)
+    sl = seq_lens
+    if sl.dtype != torch.int32 or not sl.is_contiguous():
+        sl = sl.to(torch.int32).contiguous()
+    if q.stride(2) != 1:
+        q = q.contiguous()
+    bt = block_tables if block_tables.stride(-1) == 1 else block_tables.contiguous()
+    dev = q.device
+    ws = _lib.workspace(dev, B, H, kv, D)
+    rc = L.slmt_paged_append_decode(
+        _lib.ptr(q), _lib.dtype_tag(q.dtype), q.stride(0), q.stride(1),
+        _lib.ptr(new_key), _lib.ptr(new_value), _lib.dtype_tag(new_key.dtype), new_key.stride(0),
+        _lib.ptr(kv_cache), kv_cache.size(0), bs, kv, D,
+        _lib.ptr(bt), _lib.dtype_tag(bt.dtype), bt.stride(0), bt.size(-1),
+        _lib.ptr(sl), int(max_seq_len or 0), B, H,
+        float(1.0 / math.sqrt(D) if sm_scale is None else sm_scale),
+        _lib.ptr(out), _lib.dtype_tag(out.dtype), out.stride(0), out.stride(1),
+        _lib.ptr(ws), ws.numel(), _lib.ptr(_lib.error_word(dev)), _lib.stream_of(dev))
+    _lib.check(rc, "append-decode")
     return out
 
 

@@ -142,3 +142,54 @@ def test_per_token_contiguous_decode():
         want = oracle.pt_decode(q.view(1, h, d), kp[None], kmin[None], kstep[None], vp[None], vmin[None],
                                 vstep[None])[0]
         assert_close(out[:, 0].cpu().numpy(), want, what=f"per-token d={d}")
+
+
+@pytest.mark.parametrize("d", [128, 64])
+def test_per_channel_decode_c2_full_batch_ragged(d):
+    """BASELINE config 2 at its own batch (B=16, Hq32/Hkv8, S=2048) with
+    ragged lengths: the grid and split geometry of the benchmarked launch."""
+    kd = _kd()
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(100 + d)
+    B, H, KV, S = 16, 32, 8, 2048
+    q = torch.randn(B, H, d, generator=g).half()
+    k = torch.randn(B, KV, S, d, generator=g).half()
+    v = torch.randn(B, KV, S, d, generator=g).half()
+    kp, ks, kz = kd.kv_quantize_per_channel(k.to(dev))
+    vp, vs, vz = kd.kv_quantize_per_channel(v.to(dev))
+    lens = torch.randint(1, S + 1, (B,), generator=g, dtype=torch.int32)
+    lens[:3] = torch.tensor([S, 1, 32], dtype=torch.int32)
+    for sl in (None, lens):  # every sequence full (the benchmarked launch), then ragged
+        out = kd.kv_dequant_decode_attention_batched(q.to(dev), kp, ks, kz, vp, vs, vz,
+                                                     seq_lens=None if sl is None else sl.to(dev))
+        want = oracle.pc_decode(q, kp.cpu(), ks.cpu(), kz.cpu(), vp.cpu(), vs.cpu(), vz.cpu(), seq_lens=sl)
+        assert_close(out.cpu().numpy(), want, what=f"c2 B=16 d={d} {'ragged' if sl is not None else 'full'}")
+    assert kd.read_device_errors(dev) == 0
+
+
+def test_per_token_contiguous_matches_reference_live():
+    """A/B of the contiguous per-token decode against the reference's own
+    kernel (kv_dequant_decode_per_token_attention_cuda, built unmodified into
+    oracle/_ref), on codes and rulers as its quantizer would write them."""
+    from oracle.build_ref import load_ref
+    ref = load_ref()
+    if ref is None:
+        pytest.skip("reference extension not built (python -m oracle.build_ref /path/to/slm-turbo)")
+    kd = _kd()
+    dev = torch.device("cuda")
+    for d, h, kv, s in ((128, 32, 8, 1000), (64, 32, 4, 512), (80, 8, 2, 45), (128, 16, 16, 77)):
+        g = torch.Generator().manual_seed(7 * s + d)
+        q = torch.randn(h, 1, d, generator=g).half().to(dev)
+        # per-token rulers from real rows: store each row through the paged
+        # quantizer (bit-exact to the reference's) and split the slots
+        x_k = torch.randn(s, kv, d, generator=g).half().to(dev)
+        x_v = torch.randn(s, kv, d, generator=g).half().to(dev)
+        cache = torch.zeros(s, 1, kv, d + 8, dtype=torch.uint8, device=dev)
+        kd.kv_quantize_store(x_k, x_v, cache, torch.arange(s, device=dev), 1)
+        slot = cache[:, 0].permute(1, 0, 2).contiguous()  # [kv, s, d+8]
+        kp, vp = slot[..., :d // 2].contiguous(), slot[..., d // 2:d].contiguous()
+        rul = slot[..., d:].contiguous().view(torch.float16)  # [kv, s, 4]
+        kmin, kstep, vmin, vstep = (rul[..., i].contiguous() for i in range(4))
+        ours = kd.kv_dequant_decode_per_token_attention(q, kp, kmin, kstep, vp, vmin, vstep, num_kv_heads=kv)
+        theirs = ref.kv_dequant_decode_per_token_attention_cuda(q, kp, kmin, kstep, vp, vmin, vstep, 64, kv)
+        assert_close(ours.cpu().numpy(), theirs.cpu().numpy(), what=f"per-token d={d} h={h} kv={kv} s={s}")

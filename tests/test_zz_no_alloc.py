@@ -85,3 +85,41 @@ def test_noalloc_reset_and_limit():
     rc = lib.slmt_paged_decode_noalloc(*a, 0, _lib.ptr(err), stream)
     assert rc == SCRATCH_LIMIT_STATUS
     assert b"static" in lib.slmt_status_string(rc)
+
+
+def test_noalloc_reset_recovers_after_a_failed_call():
+    """The recovery path the header documents: a call that set an error bit
+    leaves the static scratch's counters dirty; the next call passes
+    reset_scratch=1 and is right again.  The failed call is made with the
+    library's bounded-wait test hook (CTA 0's consumers wait on a barrier
+    nothing completes, 2 ms limit), so nothing faults or hangs."""
+    from slm_turbo_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    t = _case(dev)
+    B, hq, d = t["q"].shape
+    stream = _lib.stream_of(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    need = int(lib.slmt_decode_workspace_bytes(B, hq, 8, d, dev.index))
+    ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+    want = torch.empty(B, hq, d, dtype=torch.float32, device=dev)
+    assert lib.slmt_paged_decode(*_args(t, want), _lib.ptr(ws), need, _lib.ptr(err), stream) == 0
+
+    prev = lib.slmt_set_wait_limit_ns(2_000_000)
+    lib.slmt_set_debug_stall(1)
+    try:
+        junk = torch.empty_like(want)
+        assert lib.slmt_paged_decode_noalloc(*_args(t, junk), 0, _lib.ptr(err), stream) == 0
+        torch.cuda.synchronize(dev)
+    finally:
+        lib.slmt_set_debug_stall(0)
+        lib.slmt_set_wait_limit_ns(prev)
+    assert int(err.item()) & 4, "the stalled call should report the timeout bit"
+    err.zero_()
+    for call, reset in enumerate((1, 0)):
+        got = torch.full_like(want, float("nan"))
+        assert lib.slmt_paged_decode_noalloc(*_args(t, got), reset, _lib.ptr(err), stream) == 0
+        torch.cuda.synchronize(dev)
+        assert int(err.item()) == 0, f"call {call}: device error bits {int(err.item())}"
+        assert_close(got.cpu().numpy(), want.cpu().numpy(), rtol=1e-5, atol=1e-6,
+                     what=f"no-alloc call {call} after the failed one (reset_scratch={reset})")
