@@ -12,6 +12,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
@@ -20,8 +21,11 @@ CSRC = HERE / "csrc"
 INCLUDE = ROOT / "include"
 LIB_NAME = "libslm_turbo_b200.so"
 LIB_PATH = HERE / LIB_NAME
-SOURCES = ["decode.cu", "store.cu", "decode_noalloc.cu"]
-HEADERS = ["ptx.cuh", "decode_common.cuh", "decode_kernels.cuh", "quant_store.cuh", "internal.h"]
+SOURCES = ["decode.cu", "store.cu", "decode_noalloc.cu",
+           "decode_d64_paged.cu", "decode_d64_contig.cu", "decode_d80_paged.cu", "decode_d80_contig.cu",
+           "decode_d128_paged.cu", "decode_d128_contig.cu"]
+HEADERS = ["ptx.cuh", "decode_common.cuh", "decode_kernels.cuh", "decode_dispatch.cuh", "quant_store.cuh",
+           "internal.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -49,17 +53,30 @@ def build_library(force: bool = False, verbose: bool = False, extra_flags=None) 
     """Compile every .cu source into one shared library (skips if up to date)."""
     if not force and not _stale():
         return LIB_PATH
-    objs = []
     build_dir = HERE / "_build"
     build_dir.mkdir(exist_ok=True)
     flags = NVCC_FLAGS + list(extra_flags or [])
+    cmds = []
     for src in SOURCES:
         obj = build_dir / (Path(src).stem + ".o")
-        cmd = [nvcc(), *flags, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(CSRC / src), "-o", str(obj)]
+        cmds.append(([nvcc(), *flags, "-I", str(INCLUDE), "-I", str(CSRC), "-c", str(CSRC / src), "-o", str(obj)],
+                     str(obj)))
+
+    def compile_one(cmd):
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
-        objs.append(str(obj))
+        return subprocess.run(cmd, capture_output=not verbose, text=True)
+
+    # the translation units are independent: compile them in parallel
+    with ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as ex:
+        results = list(ex.map(compile_one, [c for c, _ in cmds]))
+    for (cmd, _), res in zip(cmds, results):
+        if res.returncode != 0:
+            sys.stderr.write((res.stdout or "") + (res.stderr or ""))
+            raise subprocess.CalledProcessError(res.returncode, cmd, res.stdout, res.stderr)
+        if not verbose and extra_flags and res.stderr:
+            sys.stderr.write(res.stderr)
+    objs = [o for _, o in cmds]
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "shared",
            "-Xlinker", "-rpath,/usr/local/cuda/lib64", *objs, "-o", str(tmp)]

@@ -18,51 +18,14 @@ constexpr int kSmemReserved = 1024;    // reserved per resident CTA
 
 inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
-using DecodeFn = void (*)(const DecodeParams);
-
-// The paged layout is instantiated per kv heads per stage row (KVC), so the
-// consumers' row addresses are compile-time offsets; the contiguous layouts
-// address rows with a per-warp base and need no such specialisation.
-template <int D, int NT, int KVC, bool PK>
-DecodeFn decode_fn_kvc(int layout, bool append) {
-  switch (layout) {
-    case LAYOUT_PAGED:
-      return append ? decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, true>
-                    : decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, false>;
-    case LAYOUT_PER_CHANNEL:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_CHANNEL, KVC, PK>;
-    default:
-      return decode_splitk_kernel<D, NT, LAYOUT_PER_TOKEN, KVC, PK>;
-  }
-}
-
-// Instantiated per head dim, n-tiles, kv heads per CTA (compile-time row
-// strides, one consumer warp per kv head) and tile packing (PK: at most 4
-// query heads per kv head, so two tiles share one n-tile).
-template <int D, int NT, bool PK>
-DecodeFn decode_fn_layout(int layout, int kvc, bool append) {
-  switch (kvc) {
-    case 8:
-      return decode_fn_kvc<D, NT, 8, PK>(layout, append);
-    case 4:
-      return decode_fn_kvc<D, NT, 4, PK>(layout, append);
-    case 2:
-      return decode_fn_kvc<D, NT, 2, PK>(layout, append);
-    default:
-      return decode_fn_kvc<D, NT, 1, PK>(layout, append);
-  }
-}
-
-template <int D>
-DecodeFn decode_fn_d(int nt, bool pk, int layout, int kvc, bool append) {
-  if (nt == 2) return decode_fn_layout<D, 2, false>(layout, kvc, append);
-  return pk ? decode_fn_layout<D, 1, true>(layout, kvc, append) : decode_fn_layout<D, 1, false>(layout, kvc, append);
-}
-
+// One translation unit per (head dim, layout family) instantiates the
+// kernels and returns the one a call needs (decode_d*.cu); this file
+// instantiates none, so the library's sources compile in parallel.
 DecodeFn decode_fn(int D, int nt, bool pk, int layout, int kvc, bool append) {
-  if (D == 64) return decode_fn_d<64>(nt, pk, layout, kvc, append);
-  if (D == 80) return decode_fn_d<80>(nt, pk, layout, kvc, append);
-  return decode_fn_d<128>(nt, pk, layout, kvc, append);
+  const bool paged = layout == LAYOUT_PAGED;
+  if (D == 64) return paged ? decode_fn_64_paged(nt, pk, kvc, append) : decode_fn_64_contig(nt, pk, layout, kvc);
+  if (D == 80) return paged ? decode_fn_80_paged(nt, pk, kvc, append) : decode_fn_80_contig(nt, pk, layout, kvc);
+  return paged ? decode_fn_128_paged(nt, pk, kvc, append) : decode_fn_128_contig(nt, pk, layout, kvc);
 }
 
 struct OccEntry {
@@ -515,7 +478,9 @@ int paged_decode_impl(
     if (!new_key || !new_value || !seq_lens) return SLMT_ERR_NULL;
     if (kv_dtype != SLMT_DTYPE_F16 && kv_dtype != SLMT_DTYPE_BF16) return SLMT_ERR_DTYPE;
     if (new_seq_stride < num_kv_heads * head_dim) return SLMT_ERR_SHAPE;
-    if ((reinterpret_cast<uintptr_t>(new_key) | reinterpret_cast<uintptr_t>(new_value)) % 2 != 0)
+    // rows are read two values per 32-bit word
+    if ((reinterpret_cast<uintptr_t>(new_key) | reinterpret_cast<uintptr_t>(new_value)) % 4 != 0 ||
+        new_seq_stride % 2 != 0)
       return SLMT_ERR_ALIGN;
     p.append = 1;
     p.new_bf16 = kv_dtype == SLMT_DTYPE_BF16;

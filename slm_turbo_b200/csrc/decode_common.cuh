@@ -14,6 +14,7 @@ __host__ __device__ constexpr int ctas_per_sm(int kvc, int nt) {
   return ((nt == 1) ? 18 : 9) / (kvc + 1) > 0 ? ((nt == 1) ? 18 : 9) / (kvc + 1) : 1;
 }
 constexpr int kMaxStages = 8;
+constexpr int kMaxEnds = 8;  // segment ends per range whose new token is quantized at the start
 constexpr int kTileTokens = 16;   // one m16 tensor-core tile of tokens
 constexpr int kChunkTokens = 32;  // one pipeline stage = two tiles
 constexpr uint64_t kDefaultWaitLimitNs = 4000000000ull;  // 4 s per wait (host-settable)
@@ -47,8 +48,8 @@ constexpr int kFlagFirst = 1;     // first chunk of the segment in this CTA
 constexpr int kFlagLast = 2;      // last chunk of the segment in this CTA
 constexpr int kFlagQbuf = 4;      // q buffer index (0/1)
 constexpr int kFlagRangeEnd = 8;  // last chunk of this CTA's range
-constexpr int kFlagSegEnd = 16;   // final chunk of the segment (holds its newest token)
-constexpr int kFlagOwnsEnd = 32;  // with kFlagFirst: this CTA's range holds the final chunk
+constexpr int kFlagPatch = 16;  // fused append: the range's first segment end, whose new slot
+                                // the consumers quantized at the start (hdr->newslot)
 
 // The split segment this CTA helps merge after its main loop: the segment
 // its range ends in.  Every CTA whose range ends inside a split segment
@@ -64,12 +65,17 @@ struct SmemHeader {
   uint64_t qfull[2];
   uint64_t qempty[2];
   uint64_t never;  // a barrier nothing arrives on (the stalled-consumer test hook)
-  // fused append: the new token's slot per consumer warp (kv head), quantized
-  // at the segment's start in this CTA and copied over the stale staged row
-  // when the segment's final chunk arrives
+  // fused append: the new token's slot of the range's first segment per
+  // consumer warp (kv head), quantized when the launch starts and copied over
+  // the stale staged row when the segment's final chunk arrives
   uint8_t newslot[8][136];
-  uint64_t prologue;  // fused append: the producer published its first segment
-  int pro_seq, pro_kg, pro_len;  // that segment if its final chunk is in range (pro_seq -1: none)
+  // fused append: the producer publishes the segments whose final chunk lies
+  // in this CTA's range (up to kMaxEnds, in range order); the consumer warps
+  // quantize their new tokens when the launch starts and arrive on `appended`
+  uint64_t prologue;
+  uint64_t appended;
+  int n_end;
+  int end_seq[kMaxEnds], end_kg[kMaxEnds], end_len[kMaxEnds];
   ChunkDesc desc[kMaxStages];
   int has_job;
   int merge_ok;
@@ -143,6 +149,19 @@ struct DecodeParams {
   int out_dtype;  // 0 f16, 1 bf16, 2 f32
   int64_t out_seq_stride, out_head_stride;
 };
+
+// Host-side handle of one decode kernel instantiation.
+using DecodeFn = void (*)(const DecodeParams);
+
+// Per head dim: the kernel for n-tiles nt, tile packing pk, kv heads per CTA
+// kvc, and (paged) whether the launch appends or (contiguous) the layout.
+// Defined in decode_d64.cu, decode_d80.cu, decode_d128.cu.
+DecodeFn decode_fn_64_paged(int nt, bool pk, int kvc, bool append);
+DecodeFn decode_fn_80_paged(int nt, bool pk, int kvc, bool append);
+DecodeFn decode_fn_128_paged(int nt, bool pk, int kvc, bool append);
+DecodeFn decode_fn_64_contig(int nt, bool pk, int layout, int kvc);
+DecodeFn decode_fn_80_contig(int nt, bool pk, int layout, int kvc);
+DecodeFn decode_fn_128_contig(int nt, bool pk, int layout, int kvc);
 
 __host__ __device__ inline int nchunks_of(int len) {
   return (len + kChunkTokens - 1) / kChunkTokens;

@@ -1,0 +1,9 @@
+// decode_d64_paged.cu -- decode_splitk_kernel instantiations for head dim 64,
+// paged per-token layout (plain and fused-append).
+#include "decode_dispatch.cuh"
+
+namespace slmt {
+
+DecodeFn decode_fn_64_paged(int nt, bool pk, int kvc, bool append) { return paged_fn_d<64>(nt, pk, kvc, append); }
+
+}  // namespace slmt

@@ -222,6 +222,32 @@ __device__ __forceinline__ bool next_segment(const DecodeParams& p, int s, int k
   return true;
 }
 
+// Fused append, done by the producer warp for a segment end beyond the
+// kMaxEnds that the consumers quantize at the start (only ranges that hold
+// more than kMaxEnds segment ends, i.e. very short sequences, get here):
+// quantize the new token (position t) of sequence `seq` for every kv head of
+// group kg into its cache slot before the copy of that final chunk is issued.
+// One head at a time, to keep the producer's registers free.
+template <int D>
+__device__ __noinline__ void producer_append(const DecodeParams& p, int seq, int kg, int t) {
+  const int lane = threadIdx.x & 31;
+  const int64_t ph = block_entry(p, seq, t / p.block_size);
+  const bool ok = ph >= 0 && ph < p.num_blocks;
+  if (!ok && lane == 0) set_err(p, 1u);
+  for (int j = 0; j < p.kvc; ++j) {
+    const int h = kg * p.kvc + j;
+    const int64_t off = ((int64_t)seq * p.new_seq_stride + (int64_t)h * D) * 2;  // bytes
+    const SlotRow r = quantize_slot_row<D>(reinterpret_cast<const uint8_t*>(p.new_k) + off,
+                                           reinterpret_cast<const uint8_t*>(p.new_v) + off, p.new_bf16);
+    if (ok)
+      write_slot_row<D>(const_cast<uint8_t*>(p.cache) +
+                            ((ph * p.block_size + t % p.block_size) * p.kv_total + h) * (int64_t)(D + 8),
+                        r);
+  }
+  fence_proxy_async_global();  // the copy about to be issued reads these bytes through the async proxy
+  __syncwarp();
+}
+
 template <int D, int LAYOUT, bool APPEND>
 __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
                                 uint8_t* qbuf, uint8_t* rbuf, uint8_t* stg) {
@@ -291,16 +317,35 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     int L = seq_len_of(p, s);
     int nch = nchunks_of(L);
     if constexpr (APPEND) {
-      // publish the range's first segment: its consumers quantize its new
-      // token now, while the first copies are in flight, if this range holds
-      // the segment's final chunk
+      // publish the segments whose final chunk lies in this range: the
+      // consumer warps quantize their new tokens now, while the first copies
+      // are in flight
+      int n_end = 0;
+      int es = s, ekg = kg, eL = L;
+      long long e_last = t_begin - chunk + nch - 1;  // global index of the segment's final chunk
+      while (n_end < kMaxEnds && e_last < t_end) {
+        if (lane == 0) {
+          hdr->end_seq[n_end] = es;
+          hdr->end_kg[n_end] = ekg;
+          hdr->end_len[n_end] = eL;
+        }
+        ++n_end;
+        int s2 = es, kg2 = ekg, L2 = 0;
+        bool have = false;
+        while (!have && kg2 < p.ngroups) have = next_segment(p, s2, kg2, s2, kg2, L2);
+        if (!have || kg2 >= p.ngroups) break;
+        es = s2;
+        ekg = kg2;
+        eL = L2;
+        e_last += nchunks_of(L2);
+      }
+      __syncwarp();
       if (lane == 0) {
-        hdr->pro_seq = (t_begin - chunk + nch - 1 < t_end) ? s : -1;
-        hdr->pro_kg = kg;
-        hdr->pro_len = L;
+        hdr->n_end = n_end;
         mbar_arrive(&hdr->prologue);
       }
     }
+    int ends_passed = 0;  // final chunks issued so far
     bool first = true;
     uint32_t seg = 0;  // segments started by this CTA
     int seg_ncov = 1, seg_cfirst = c, seg_mergers = 0;
@@ -346,10 +391,25 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       const int nvalid = min(kChunkTokens, L - chunk * kChunkTokens);
       int flags = (first ? kFlagFirst : 0) | (last ? kFlagLast : 0) | (qb ? kFlagQbuf : 0) |
                   (t == t_end - 1 ? kFlagRangeEnd : 0);
-      bool owns_end = false;
       if constexpr (APPEND) {
-        owns_end = first && (t - chunk + nch - 1 < t_end);
-        flags |= (chunk == nch - 1 ? kFlagSegEnd : 0) | (owns_end ? kFlagOwnsEnd : 0);
+        if (chunk == nch - 1) {
+          if (ends_passed == 0) {
+            // the consumers quantized this one at the start, possibly after
+            // the copy below reads the slot: they patch the staged row
+            flags |= kFlagPatch;
+          } else if (ends_passed < hdr->n_end) {
+            // quantized at the start too: wait until those slots are written
+            // before the copy below reads them
+            if (ends_passed == 1 && !mbar_wait(&hdr->appended, 0u, p.wait_limit_ns)) {
+              failed = true;
+              break;
+            }
+          } else {
+            // beyond the published ends: quantize it here
+            producer_append<D>(p, s, kg, L - 1);
+          }
+          ++ends_passed;
+        }
       }
       const int slot = (int)(c + (int64_t)kg * B + s);
       uint8_t* dst = stg + (size_t)stage * p.stage_bytes;
@@ -482,16 +542,6 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       }
       cp_async_arrive_noinc(fb);
 
-      if (APPEND && owns_end) {
-        // the consumers quantize the group's new K/V rows when this segment
-        // starts: pull them into L2 now (one 128-byte line per lane)
-        const int64_t row0 = (int64_t)s * p.new_seq_stride + (int64_t)kg * p.kvc * D;
-        const int lines = (p.kvc * D * 2 + 127) / 128;
-        for (int i = lane; i < 2 * lines; i += 32) {
-          const void* base = (i < lines) ? p.new_k : p.new_v;
-          prefetch_l2(reinterpret_cast<const uint8_t*>(base) + row0 * 2 + (int64_t)(i % lines) * 128);
-        }
-      }
       if (first) {
         // ---- q (raw fp16/bf16) and per-channel rulers of this segment, staged
         // after the segment's first chunk is already in flight ----
@@ -580,7 +630,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
 
   if constexpr (APPEND) {
     if (t_begin >= t_end && lane == 0) {  // empty range: nothing to publish
-      hdr->pro_seq = -1;
+      hdr->n_end = 0;
       mbar_arrive(&hdr->prologue);
     }
   }
@@ -1023,12 +1073,13 @@ __device__ __forceinline__ void fold_v_bias(WarpState<D, NT>& w) {
 
 // Fused append (paged layout): kv head h's new row of sequence `seq` (its
 // newest token, position t = len-1) is quantized by this warp with the store
-// kernel's arithmetic; the slot goes to the cache (for later launches) and to
+// kernel's arithmetic; the slot goes to the cache and, when `keep` (the
+// range's first segment end, whose copy may already be in flight), to
 // hdr->newslot[j], which replaces the stale staged copy of the slot when the
 // segment's final chunk arrives.
 template <int D, int KVC>
 __device__ __forceinline__ void append_token(const DecodeParams& p, SmemHeader* hdr, int seq, int h, int t,
-                                             int j) {
+                                             int j, bool keep) {
   const int lane = threadIdx.x & 31;
   const int64_t ph = block_entry(p, seq, t / p.block_size);
   const int64_t off = ((int64_t)seq * p.new_seq_stride + (int64_t)h * D) * 2;  // bytes
@@ -1040,7 +1091,7 @@ __device__ __forceinline__ void append_token(const DecodeParams& p, SmemHeader* 
                       nr);
   else if (lane == 0)
     set_err(p, 1u);
-  write_slot_row<D>(hdr->newslot[j], nr);
+  if (keep) write_slot_row<D>(hdr->newslot[j], nr);
   __syncwarp();
 }
 
@@ -1070,7 +1121,6 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
   };
 
   bool run = true;
-  bool pre_done = false;  // the range's first segment's new token is quantized
   if (p.debug_stall && blockIdx.x == 0) {
     // Test hook (off unless the host sets it): CTA 0's consumer warps wait
     // for a barrier phase that nothing completes, so the wait runs out after
@@ -1080,15 +1130,21 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
   }
 
   if constexpr (APPEND) {
-    // Fused append, first segment of the range: quantize its new token while
-    // the producer's first copies are in flight.
+    // Fused append: quantize the new tokens of the segments whose final chunk
+    // this CTA decodes (kv head j each), while the producer's first copies
+    // are in flight; then let the producer copy those final chunks.
     if (run) {
       if (!mbar_wait(&hdr->prologue, 0u, p.wait_limit_ns)) {
         give_up();
         run = false;
-      } else if (hdr->pro_seq >= 0) {
-        append_token<D, KVC>(p, hdr, hdr->pro_seq, hdr->pro_kg * kvc + j, hdr->pro_len - 1, j);
-        pre_done = true;
+      } else {
+        const int n_end = hdr->n_end;
+        for (int e = 0; e < n_end; ++e)
+          append_token<D, KVC>(p, hdr, hdr->end_seq[e], hdr->end_kg[e] * kvc + j, hdr->end_len[e] - 1, j,
+                               e == 0);
+        fence_proxy_async_global();  // the producer's copies read these slots through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&hdr->appended);
       }
     }
   }
@@ -1104,16 +1160,6 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
     const int flags = dsm.flags, slot = dsm.slot, nvalid = dsm.nvalid;
     const int qbi = (flags & kFlagQbuf) ? 1 : 0;
 
-    if constexpr (APPEND) {
-      if ((flags & kFlagFirst) && (flags & kFlagOwnsEnd)) {
-        // a later segment whose final chunk this CTA decodes: quantize its
-        // new token now (no softmax state is live at a segment start)
-        if (pre_done)
-          pre_done = false;  // the range's first segment: done at the start
-        else
-          append_token<D, KVC>(p, hdr, dsm.seq, dsm.kg * kvc + j, dsm.len - 1, j);
-      }
-    }
     if (flags & kFlagFirst) {
       // ---- segment start: q fragments, q sums, fresh softmax state ----
       if (!mbar_wait(&hdr->qfull[qbi], (seg / (uint32_t)p.nqbuf) & 1u, p.wait_limit_ns)) {
@@ -1193,7 +1239,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
     {
       const uint8_t* st = stg + (size_t)stage * p.stage_bytes;
       if constexpr (APPEND) {
-        if (flags & kFlagSegEnd) {
+        if (flags & kFlagPatch) {
           // the segment's newest token is the last valid row of this chunk:
           // its slot, quantized at the segment start, replaces the staged copy
           // (read from the cache before this launch wrote it)
@@ -1387,6 +1433,7 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
     }
     mbar_init(&hdr->never, 1);
     mbar_init(&hdr->prologue, 1);
+    mbar_init(&hdr->appended, KVC);
     hdr->has_job = 0;
     hdr->abort = 0;
     fence_mbar_init();

@@ -26,38 +26,14 @@ struct SlotRow {
   uint2 rulers;     // (k_min | k_step << 16, v_min | v_step << 16), fp16 bits
 };
 
-// key_row / value_row: the row's D values (fp16, or bf16 when in_bf16).
+// Quantize a row whose VEC values per lane are in xk / xv (lanes >= LANES
+// hold zeros and take no part in the min/max).
 template <int D>
-__device__ __forceinline__ SlotRow quantize_slot_row(const void* key_row, const void* value_row,
-                                                     int in_bf16) {
+__device__ __forceinline__ SlotRow quantize_slot_vals(const float (&xk)[SlotGeom<D>::VEC],
+                                                      const float (&xv)[SlotGeom<D>::VEC]) {
   constexpr int VEC = SlotGeom<D>::VEC;
   const int lane = threadIdx.x & 31;
   const bool act = lane < SlotGeom<D>::LANES;
-  float xk[VEC], xv[VEC];
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    xk[i] = 0.f;
-    xv[i] = 0.f;
-  }
-  if (act) {
-    if (in_bf16) {
-      const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(key_row) + lane * VEC;
-      const __nv_bfloat16* vp = reinterpret_cast<const __nv_bfloat16*>(value_row) + lane * VEC;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        xk[i] = __bfloat162float(kp[i]);
-        xv[i] = __bfloat162float(vp[i]);
-      }
-    } else {
-      const __half* kp = reinterpret_cast<const __half*>(key_row) + lane * VEC;
-      const __half* vp = reinterpret_cast<const __half*>(value_row) + lane * VEC;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        xk[i] = __half2float(kp[i]);
-        xv[i] = __half2float(vp[i]);
-      }
-    }
-  }
   float kmn = INFINITY, kmx = -INFINITY, vmn = INFINITY, vmx = -INFINITY;
   if (act) {
 #pragma unroll
@@ -97,6 +73,68 @@ __device__ __forceinline__ SlotRow quantize_slot_row(const void* key_row, const 
   r.rulers.y = (uint32_t)__half_as_ushort(__float2half_rn(vmn)) |
                ((uint32_t)__half_as_ushort(__float2half_rn(vst)) << 16);
   return r;
+}
+
+// This lane's VEC values of a row of D fp16 (or bf16, in_bf16) values.
+template <int D>
+__device__ __forceinline__ void load_row_vals(const void* row, int in_bf16, float (&x)[SlotGeom<D>::VEC]) {
+  constexpr int VEC = SlotGeom<D>::VEC;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) x[i] = 0.f;
+  if (lane < SlotGeom<D>::LANES) {
+    if (in_bf16) {
+      const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(row) + lane * VEC;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) x[i] = __bfloat162float(rp[i]);
+    } else {
+      const __half* rp = reinterpret_cast<const __half*>(row) + lane * VEC;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) x[i] = __half2float(rp[i]);
+    }
+  }
+}
+
+// Quantize one (token, kv head): key_row / value_row are its D values.
+template <int D>
+__device__ __forceinline__ SlotRow quantize_slot_row(const void* key_row, const void* value_row,
+                                                     int in_bf16) {
+  float xk[SlotGeom<D>::VEC], xv[SlotGeom<D>::VEC];
+  load_row_vals<D>(key_row, in_bf16, xk);
+  load_row_vals<D>(value_row, in_bf16, xv);
+  return quantize_slot_vals<D>(xk, xv);
+}
+
+// The VEC 16-bit values of this lane, packed (two per word), for rows that
+// are 4-byte aligned at every lane's offset (D = 64: 2 values; else 4).
+template <int D>
+struct PackedRow {
+  uint32_t w[SlotGeom<D>::VEC / 2];
+};
+
+template <int D>
+__device__ __forceinline__ PackedRow<D> load_row_packed(const void* row) {
+  constexpr int VEC = SlotGeom<D>::VEC;
+  const int lane = threadIdx.x & 31;
+  PackedRow<D> r;
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) r.w[i] = 0u;
+  if (lane < SlotGeom<D>::LANES) {
+    const uint32_t* rp = reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(row) + lane * VEC);
+#pragma unroll
+    for (int i = 0; i < VEC / 2; ++i) r.w[i] = rp[i];
+  }
+  return r;
+}
+
+template <int D>
+__device__ __forceinline__ void unpack_row(const PackedRow<D>& r, int in_bf16, float (&x)[SlotGeom<D>::VEC]) {
+#pragma unroll
+  for (int i = 0; i < SlotGeom<D>::VEC / 2; ++i) {
+    const uint16_t lo = (uint16_t)(r.w[i] & 0xFFFFu), hi = (uint16_t)(r.w[i] >> 16);
+    x[2 * i] = in_bf16 ? __bfloat162float(__ushort_as_bfloat16(lo)) : __half2float(__ushort_as_half(lo));
+    x[2 * i + 1] = in_bf16 ? __bfloat162float(__ushort_as_bfloat16(hi)) : __half2float(__ushort_as_half(hi));
+  }
 }
 
 // Write the row's slot at `slot` (global or shared memory; 8-byte aligned,

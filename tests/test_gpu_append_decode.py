@@ -95,3 +95,18 @@ def test_append_decode_bad_page_is_reported_not_faulted():
     torch.cuda.synchronize(dev)
     assert kd.read_device_errors(dev) & 1
     assert torch.isfinite(out[0]).all()
+
+
+def test_append_decode_many_short_sequences():
+    """4,000 sequences of at most one chunk: a CTA's range then holds more
+    segment ends than the consumers quantize at the start, so the producer's
+    path for the rest runs too."""
+    from slm_turbo_b200.kernels import kv_dequant as kd
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(31)
+    lengths = torch.randint(1, 33, (4000,), generator=g).tolist()
+    case = _case(lengths, d=64, hq=8, kv=8, seed=31)
+    c1, o1, c2, o2 = _run_both(case, dev)
+    assert kd.read_device_errors(dev) == 0
+    assert (c1 == c2).all()
+    assert_close(o2, o1, rtol=1e-5, atol=1e-6, what="many short sequences")
