@@ -46,6 +46,7 @@ SEQS_PER_GPU = 64
 HQ, HKV, D, BS = 32, 8, 128, 16
 LMIN, LMAX = 128, 8192
 SEED = 1234
+C5_SEQS, C5_LMIN, C5_LMAX, C5_STEPS = 256, 512, 4096, 128
 E2E_GRAPH_STEPS = 32  # e2e steps per captured CUDA graph (the first input and last output copy of a graph cannot overlap compute)
 DECODE_LAUNCHES = 2000  # decode-only launches timed back to back for the roofline (whatever --steps is)
 E2E_EAGER_STEPS = 500  # e2e steps issued eagerly through the public API
@@ -422,22 +423,40 @@ def run_ours(args):
         return float(t.item())
 
     # ---- warm-up, then K timed steps (device-timed, max over ranks) ----
+    # The K steps are issued as ONE replay of a CUDA graph that holds K
+    # captured calls of the public API (captured before the timed region), as
+    # a serving engine issues decode steps; every step does its full work.
+    # The same K steps issued eagerly from Python are timed too
+    # (eager_ms_per_step): there the host's per-call cost shows.
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(dev)
     assert kd.read_device_errors(dev) == 0, "device error word set during warm-up"
+    steps_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(steps_graph):
+        for _ in range(args.steps):
+            step()
+    steps_graph.replay()
+    torch.cuda.synchronize(dev)
     barrier()
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(dev.index)
     clk.__enter__()  # sampled across the K steps and the decode-only leg below
     ev0.record(stream)
+    steps_graph.replay()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    del steps_graph
+    ev0.record(stream)
     for _ in range(args.steps):
         step()
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
-    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    eager_ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
 
     # ---- dominant kernel: the decode launch alone, DECODE_LAUNCHES back to back ----
     n_dec = max(DECODE_LAUNCHES, args.steps)
@@ -580,6 +599,9 @@ def run_ours(args):
         "data": "synthetic", "config": workload_config(w, world),
         "decode_us": dec_ms * 1e3, "decode_hbm_gbs": achieved,
         "step": "one launch: new token quantized into the cache + decode (append fused)",
+        "step_issue": f"the K steps replayed from one CUDA graph of K captured public-API calls; issued "
+                      f"eagerly from Python the same K steps take {eager_ms_step * 1e3:.1f} us per step",
+        "eager_ms_per_step": eager_ms_step,
         "hbm_pct_of_8tbs": 100.0 * achieved / NOMINAL_HBM_GBS,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": profiled_traffic(dec_bytes),
@@ -760,6 +782,160 @@ def run_c4(args):
     return 0
 
 
+C5_CHILD = r"""
+import json, os, sys, time
+sys.path.insert(0, sys.argv[1])
+model_dir, mode, n_seqs, lmin, lmax, steps, seed = sys.argv[2], sys.argv[3], *map(int, sys.argv[4:9])
+import torch
+from slm_turbo_b200.adapters import vllm_adapter as ad
+ad.register_plugin()
+if mode == "refkern":
+    # the reference's own CUDA kernels (oracle/_ref), driven as its adapter
+    # drives them: one store launch, seq_lens.tolist(), one decode launch per
+    # request per layer (adapters/vllm_adapter.py:185-203, 246-284)
+    from oracle.build_ref import load_ref
+    ref = load_ref()
+    Impl = ad.QuantizedKVAttentionImpl
+    def store(self, layer, key, value, kv_cache, slot_mapping):
+        if kv_cache is not None and kv_cache.numel():
+            ref.kv_quantize_store_cuda(key.contiguous(), value.contiguous(), kv_cache, slot_mapping,
+                                       kv_cache.shape[1])
+    def decode(self, query, kv_cache, md, out, n):
+        for r, L in enumerate(md.seq_lens[:n].tolist()):
+            if L > 0:
+                o = ref.kv_dequant_decode_per_token_paged_attention_cuda(
+                    query[r:r + 1].permute(1, 0, 2).contiguous(), kv_cache,
+                    md.block_table[r].to(torch.int64).contiguous(), int(L), kv_cache.shape[1], kv_cache.shape[2])
+                out[r] = o.permute(1, 0, 2)[0].to(out.dtype)
+        return out
+    Impl.do_kv_cache_update = store
+    Impl._decode_attention = decode
+from vllm import LLM, SamplingParams
+kw = dict(model=model_dir, load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
+          attention_backend="CUSTOM", block_size=16, max_model_len=lmax + steps + 32, max_num_seqs=n_seqs,
+          max_num_batched_tokens=16384, gpu_memory_utilization=0.6, enable_prefix_caching=False, seed=0)
+if mode == "ours-graph":
+    kw.update(compilation_config={"mode": 0, "cudagraph_mode": "FULL_DECODE_ONLY",
+                                  "cudagraph_capture_sizes": [n_seqs]})
+else:
+    kw.update(enforce_eager=True)
+llm = LLM(**kw)
+g = torch.Generator().manual_seed(seed)
+lens = torch.randint(lmin, lmax + 1, (n_seqs,), generator=g).tolist()
+prompts = [{"prompt_token_ids": torch.randint(3, 32000, (L,), generator=g).tolist()} for L in lens]
+llm.generate(prompts[:4], SamplingParams(max_tokens=4, temperature=0.0, ignore_eos=True), use_tqdm=False)
+def timed(max_tokens):
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    outs = llm.generate(prompts, SamplingParams(max_tokens=max_tokens, temperature=0.0, ignore_eos=True),
+                        use_tqdm=False)
+    e1.record()
+    torch.cuda.synchronize()
+    assert all(len(o.outputs[0].token_ids) == max_tokens for o in outs)
+    return e0.elapsed_time(e1) * 1e-3, time.perf_counter() - t0
+t1, w1 = timed(1)
+t2, w2 = timed(1 + steps)
+from slm_turbo_b200.kernels import kv_dequant as kd
+err = kd.read_device_errors(torch.device("cuda", 0), reset=False)
+print("RESULT " + json.dumps({"mode": mode, "prefill_s": t1, "total_s": t2, "decode_s": t2 - t1,
+                              "wall_decode_s": w2 - w1, "ctx_tokens": sum(lens), "device_errors": err,
+                              "decode_tok_s": n_seqs * steps / (t2 - t1)}), flush=True)
+"""
+
+
+def _c5_config(d):
+    cfg = {"architectures": ["LlamaForCausalLM"], "model_type": "llama", "hidden_size": 2048,
+           "intermediate_size": 5632, "num_hidden_layers": 22, "num_attention_heads": 32,
+           "num_key_value_heads": 4, "head_dim": 64, "vocab_size": 32000, "max_position_embeddings": 8192,
+           "rms_norm_eps": 1e-5, "rope_theta": 10000.0, "hidden_act": "silu", "tie_word_embeddings": False,
+           "bos_token_id": 1, "eos_token_id": 2, "torch_dtype": "bfloat16"}
+    (Path(d) / "config.json").write_text(json.dumps(cfg))
+
+
+def c5_engine(mode, args):
+    """Run one C5 engine (a child process: its own CUDA context and vLLM
+    state) and return its RESULT dict."""
+    import subprocess
+    import tempfile
+    world, rank, local = dist_env()
+    with tempfile.TemporaryDirectory() as d:
+        _c5_config(d)
+        env = dict(os.environ, VLLM_ENABLE_V1_MULTIPROCESSING="0", CUDA_VISIBLE_DEVICES=str(local))
+        for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT", "LOCAL_WORLD_SIZE",
+                  "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID"):
+            env.pop(k, None)
+        proc = subprocess.run([sys.executable, "-c", C5_CHILD, str(ROOT), d, mode, str(C5_SEQS), str(C5_LMIN),
+                               str(C5_LMAX), str(C5_STEPS), str(SEED + 50 + rank)],
+                              env=env, capture_output=True, text=True, timeout=3000)
+    lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("RESULT ")]
+    if proc.returncode != 0 or not lines:
+        return {"mode": mode, "failed": (proc.stdout[-1500:] + proc.stderr[-2500:])}
+    return json.loads(lines[-1][len("RESULT "):])
+
+
+def run_reference_c5(args):
+    """C5 with the reference's own CUDA kernels (oracle/_ref) in the same vLLM
+    engine, driven by its adapter's per-request decode loop (eager: the loop
+    syncs seq_lens to the host every step).  Rank 0 only."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle.build_ref import built_path
+    if built_path() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference extension not built into oracle/_ref"}))
+        return 0
+    r = c5_engine("refkern", args)
+    v = r.get("decode_tok_s")
+    print(json.dumps({"metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world,
+                      "steps": C5_STEPS, "warmup": 1, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": "C5 (see the ours line); reference CUDA kernels, per-request loop"},
+                      "engine": r}), flush=True)
+    return 0
+
+
+def run_c5(args):
+    """model-level continuous-batching decode through vLLM's
+    CUSTOM backend (this package's adapter and kernels) on a random-init
+    TinyLlama-shape Llama (22 layers, hidden 2048, 32/4 heads, head_dim 64,
+    SwiGLU 5632, vocab 32000, bf16 weights), 256 requests per GPU with
+    prompt lengths U[512, 4096], 128 decode steps, block 16.  Each GPU runs
+    its own replica (data parallel; weak scaling).  decode tok/s = 256 x 128
+    / (time of generate with 129 new tokens - time with 1 new token), both
+    device-timed; the prefill is the difference's common part.  CUDA graphs
+    for the decode steps (vLLM FULL_DECODE_ONLY, no torch.compile) and, beside
+    it, the same engine eager."""
+    world, rank, local = dist_env()
+    res = {m: c5_engine(m, args) for m in ("ours-graph", "ours-eager")}
+    vals = [res[m].get("decode_tok_s") for m in res]
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        t = torch.tensor([min(res[m].get("decode_s", float("inf")) for m in res)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        slowest = float(t.item())
+        dist.destroy_process_group()
+    else:
+        slowest = min(res[m].get("decode_s", float("inf")) for m in res)
+    if rank != 0:
+        return 0
+    best = max((v for v in vals if v), default=None)
+    value = C5_SEQS * C5_STEPS * world / slowest if slowest != float("inf") else None
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": C5_STEPS, "warmup": 1,
+        "ms_per_step": slowest / C5_STEPS * 1e3 if value else None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random token ids)",
+        "config": {"workload": "C5 TinyLlama-shape model (22L, hidden 2048, 32/4 heads, D64, SwiGLU 5632, "
+                               "vocab 32000, bf16), vLLM CUSTOM backend, 256 requests/GPU, prompts U[512,4096], "
+                               "128 decode steps, block 16, 4-bit paged KV",
+                   "parallelism": f"data-parallel replicas x{world}"},
+        "best_rank0_decode_tok_s": best, "engines_rank0": res}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -768,16 +944,20 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="c3", choices=["c3", "c2", "c4"],
-                    help="c3 (default, the metric's config); c2 / c4 print extra lines")
+    ap.add_argument("--workload", default="c3", choices=["c3", "c2", "c4", "c5"],
+                    help="c3 (default, the metric's config); c2 / c4 / c5 print extra lines")
     ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128], help="c2 only")
     args = ap.parse_args()
+    if args.impl == "reference" and args.workload == "c5":
+        return run_reference_c5(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "c2":
         return run_c2(args)
     if args.workload == "c4":
         return run_c4(args)
+    if args.workload == "c5":
+        return run_c5(args)
     return run_ours(args)
 
 

@@ -111,6 +111,11 @@ def _patch_attention_layer_spec() -> bool:
     return True
 
 
+def _capturing() -> bool:
+    """True while the current CUDA stream is being captured into a graph."""
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
 class _ErrorWatch:
     """Sync-free poll of the kernels' device error word (SLMT_DEVERR_* bits).
 
@@ -124,7 +129,7 @@ class _ErrorWatch:
         self.event = None
 
     def poll(self) -> None:
-        if torch.cuda.is_current_stream_capturing():
+        if _capturing():
             return
         from slm_turbo_b200 import _lib
         if self.event is not None and self.event.query():
@@ -249,7 +254,8 @@ def _register_custom_backend() -> bool:
             bt = attn_metadata.block_table[:nreq].index_select(0, req)
             self._slm_decode_batched(
                 query, kv_cache, bt, vlen, block_size=kv_cache.shape[1], num_kv_heads=kv_cache.shape[2],
-                out=out, sm_scale=self.scale, max_seq_len=int(attn_metadata.max_seq_len))
+                out=out, sm_scale=self.scale,
+                max_seq_len=None if _capturing() else int(attn_metadata.max_seq_len))
             _KERNEL_CALLS += 1
             raw = self._first_chunk_attention(query, key, value, req)
             out.copy_(torch.where(first.view(n, 1, 1), raw.to(out.dtype), out))
@@ -278,10 +284,14 @@ def _register_custom_backend() -> bool:
         def _decode_attention(self, query, kv_cache, attn_metadata, out, n):
             """All requests of the step in one launch, output in place."""
             global _KERNEL_CALLS
+            # The longest length only sizes the grid; a CUDA graph keeps the
+            # capture-time value, so under capture the grid is sized for the
+            # block table's capacity instead.
+            hint = None if _capturing() else int(attn_metadata.max_seq_len)
             self._slm_decode_batched(
                 query, kv_cache, attn_metadata.block_table[:n], attn_metadata.seq_lens[:n],
                 block_size=kv_cache.shape[1], num_kv_heads=kv_cache.shape[2], out=out,
-                sm_scale=self.scale, max_seq_len=int(attn_metadata.max_seq_len))
+                sm_scale=self.scale, max_seq_len=hint)
             _KERNEL_CALLS += 1
             if getattr(self, "_slm_logged", False) is False:
                 self._slm_logged = True
