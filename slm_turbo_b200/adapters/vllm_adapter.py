@@ -236,6 +236,53 @@ def _register_custom_backend() -> bool:
             """Per request: raw-K/V causal attention for a request with no cached
             context (the reference's first-chunk SDPA, :230-243), the packed
             cache through the block table for every other query token."""
+            if _capturing():
+                return self._prefill_attention_device(query, key, value, kv_cache, attn_metadata, out)
+            global _KERNEL_CALLS
+            n, hq, d = query.shape
+            nreq = attn_metadata.seq_lens.shape[0]
+            # one host read of the step's request offsets (eager steps only;
+            # under graph capture the all-device path above runs)
+            qsl = attn_metadata.query_start_loc[:nreq + 1].tolist()
+            seq_lens = attn_metadata.seq_lens[:nreq].tolist()
+            cached_rows, cached_lens, cached_req = [], [], []
+            hk = key.shape[1]
+            for r in range(nreq):
+                a, b = qsl[r], min(qsl[r + 1], n)
+                if b <= a:
+                    continue
+                ctx = seq_lens[r] - (qsl[r + 1] - qsl[r])
+                if ctx <= 0:  # all of this request's tokens are new: causal over them
+                    o = torch.nn.functional.scaled_dot_product_attention(
+                        query[a:b].transpose(0, 1).unsqueeze(0), key[a:b].transpose(0, 1).unsqueeze(0),
+                        value[a:b].transpose(0, 1).unsqueeze(0), is_causal=True, scale=self.scale,
+                        enable_gqa=hk < hq)
+                    out[a:b] = o[0].transpose(0, 1).to(out.dtype)
+                else:  # token j attends to positions 0..ctx+j of the packed cache
+                    cached_rows.append((a, b))
+                    cached_lens.append((ctx + 1, ctx + 1 + (b - a)))
+                    cached_req.append(r)
+            if cached_rows:
+                dev = query.device
+                rows = torch.cat([torch.arange(a, b) for a, b in cached_rows]).to(dev)
+                lens = torch.cat([torch.arange(l0, l1, dtype=torch.int32) for l0, l1 in cached_lens]).to(dev)
+                reqs = torch.cat([torch.full((b - a,), r, dtype=torch.long)
+                                  for (a, b), r in zip(cached_rows, cached_req)]).to(dev)
+                bt = attn_metadata.block_table[:nreq].index_select(0, reqs)
+                sub = torch.empty(rows.numel(), hq, d, dtype=out.dtype, device=dev)
+                self._slm_decode_batched(
+                    query.index_select(0, rows), kv_cache, bt, lens, block_size=kv_cache.shape[1],
+                    num_kv_heads=kv_cache.shape[2], out=sub, sm_scale=self.scale,
+                    max_seq_len=max(l1 for _, l1 in cached_lens) - 1)
+                out.index_copy_(0, rows, sub)
+                _KERNEL_CALLS += 1
+            return out
+
+        def _prefill_attention_device(self, query, key, value, kv_cache, attn_metadata, out):
+            """The same computation with no host read (used under CUDA graph
+            capture): every token is a pseudo-sequence of the packed-cache
+            kernel (length 0 for requests without cached context), and a
+            block-diagonal causal SDPA over the raw K/V covers the others."""
             global _KERNEL_CALLS
             n, hq, d = query.shape
             dev = query.device
@@ -248,23 +295,20 @@ def _register_custom_backend() -> bool:
             ctx = seq_lens - (qsl[1:] - qsl[:-1])       # cached tokens before this step's chunk
             pos = ctx[req] + (tok - qsl[req])           # absolute position of each query token
             first = ctx[req] <= 0                       # request with no cached context
-            # every query token with cached context is a pseudo-sequence of
-            # length pos+1 over its request's pages; the others get length 0
             vlen = torch.where(first, torch.zeros_like(pos), pos + 1).to(torch.int32)
             bt = attn_metadata.block_table[:nreq].index_select(0, req)
             self._slm_decode_batched(
                 query, kv_cache, bt, vlen, block_size=kv_cache.shape[1], num_kv_heads=kv_cache.shape[2],
-                out=out, sm_scale=self.scale,
-                max_seq_len=None if _capturing() else int(attn_metadata.max_seq_len))
+                out=out, sm_scale=self.scale, max_seq_len=None)
             _KERNEL_CALLS += 1
             raw = self._first_chunk_attention(query, key, value, req)
             out.copy_(torch.where(first.view(n, 1, 1), raw.to(out.dtype), out))
             return out
 
         def _first_chunk_attention(self, query, key, value, req):
-            """Causal attention of each request over its own raw K/V (the
-            reference's prefill restricted to one request), in blocks of
-            query rows so the mask stays small."""
+            """Causal attention of each request over its own raw K/V, as one
+            block-diagonal masked SDPA over the step's tokens in blocks of
+            query rows (no host read; used under capture)."""
             n, hq, d = query.shape
             hk = key.shape[1]
             if hk != hq:

@@ -123,6 +123,27 @@ bool encode_codes_map(CUtensorMap* m, const uint8_t* base, int64_t num_seqs, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tensor map of the paged pool [num_blocks*block_size rows][kv*(D+8) bytes]
+// viewed as 8-byte elements, box = 16 rows x kvc heads: one tiled copy moves
+// a 16-token page tile of a kv group whose heads are a part of each row.
+// False unless every rule of the tiled copy holds (16-byte aligned base and
+// row stride, box row a multiple of 16 bytes, box within 256 elements, row
+// count within the 32-bit coordinate range).
+bool encode_pool_map(CUtensorMap* m, const uint8_t* base, int64_t rows, int64_t kv, int64_t D, int kvc) {
+  auto enc = tensor_map_encoder();
+  const int64_t slot = D + 8;
+  if (!enc || reinterpret_cast<uintptr_t>(base) % 16 != 0 || slot % 8 != 0) return false;
+  if ((kv * slot) % 16 != 0 || (kvc * slot) % 16 != 0 || kvc * slot / 8 > 256) return false;
+  if (rows < 16 || rows > INT32_MAX) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)(kv * slot / 8), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(kv * slot)};
+  const cuuint32_t box[2] = {(cuuint32_t)(kvc * slot / 8), (cuuint32_t)kTileTokens};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct Geometry {
   int G, nt, kvc, ngroups;
   bool pk;  // two tiles share one n-tile (G <= 4)
@@ -470,6 +491,9 @@ int paged_decode_impl(
   p.max_blocks = (int)max_blocks_per_seq;
   if (geo.kvc == num_kv_heads && block_size % 16 == 0 && ca % 16 == 0)
     p.paged_mode = 0;
+  else if (block_size % 16 == 0 &&
+           encode_pool_map(&p.tmap_k, kv_cache, num_blocks * block_size, num_kv_heads, head_dim, geo.kvc))
+    p.paged_mode = 3;
   else if ((geo.kvc * slot) % 16 == 0 && (num_kv_heads * slot) % 16 == 0 && ca % 16 == 0)
     p.paged_mode = 1;
   else

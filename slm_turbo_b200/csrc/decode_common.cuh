@@ -104,7 +104,8 @@ struct DecodeParams {
   int bt_i64;
   int64_t bt_seq_stride;
   int max_blocks;
-  int paged_mode;  // 0: one bulk copy per 16-token tile, 1: bulk copy per row, 2: cp.async rows
+  int paged_mode;  // 0: one bulk copy per 16-token tile, 1: bulk copy per row, 2: cp.async rows,
+                   // 3: one 2-D tiled copy per 16-token tile of the group's heads (tmap_k)
   // contiguous layouts
   const uint8_t* k_codes;
   const uint8_t* v_codes;
@@ -119,7 +120,9 @@ struct DecodeParams {
   // contiguous layouts: K and V codes [B, KV, S*D/2 bytes] as 3-D tensor
   // maps of 8-byte elements with a box of one chunk of a kv group, so a
   // chunk's K (or V) rows of every kv head of the group arrive with one
-  // tiled TMA copy; used when tma_tensor is set
+  // tiled TMA copy; used when tma_tensor is set.  Paged layout, mode 3:
+  // tmap_k views the pool as [num_blocks*block_size token rows][kv_total*
+  // (D+8) bytes as 8-byte elements] with a box of 16 rows x the group's heads
   int tma_tensor;
   CUtensorMap tmap_k, tmap_v;
   // lengths

@@ -352,7 +352,8 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
 
     // prefetched state: page-id windows of this segment (current, next) and
     // the next segment's length and first window
-    const bool pg_mode0 = (LAYOUT == LAYOUT_PAGED) && p.paged_mode == 0;
+    // whole 16-token tiles per copy (mode 0: contiguous bulk; mode 3: 2-D tiled)
+    const bool pg_mode0 = (LAYOUT == LAYOUT_PAGED) && (p.paged_mode == 0 || p.paged_mode == 3);
     int pg_base = 2 * chunk;
     int64_t pg_cur = 0, pg_nxt = 0, pg_seg = 0;
     int ns = 0, nkg = 0, nL = 0;
@@ -442,13 +443,21 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           __syncwarp();
           if (lane == 0) {
             mbar_arrive_expect_tx(fb, tx);
-            if (ok0)
-              bulk_g2s(dst, p.cache + ((ph0 * bs + tok0 % bs) * p.kv_total) * (int64_t)SLOT, tile_bytes, fb,
-                       policy);
-            if (ok1)
-              bulk_g2s(dst + tile_bytes,
-                       p.cache + ((ph1 * bs + (tok0 + kTileTokens) % bs) * p.kv_total) * (int64_t)SLOT,
-                       tile_bytes, fb, policy);
+            if (p.paged_mode == 3) {
+              // the group's heads of 16 token rows: x = first 8-byte element of
+              // head kg*kvc in a row (a multiple of 16 bytes), y = token row
+              const int x = kg * p.kvc * (SLOT / 8);
+              if (ok0) tma_load_2d(dst, &p.tmap_k, x, (int)(ph0 * bs + tok0 % bs), fb);
+              if (ok1) tma_load_2d(dst + tile_bytes, &p.tmap_k, x, (int)(ph1 * bs + (tok0 + kTileTokens) % bs), fb);
+            } else {
+              if (ok0)
+                bulk_g2s(dst, p.cache + ((ph0 * bs + tok0 % bs) * p.kv_total) * (int64_t)SLOT, tile_bytes, fb,
+                         policy);
+              if (ok1)
+                bulk_g2s(dst + tile_bytes,
+                         p.cache + ((ph1 * bs + (tok0 + kTileTokens) % bs) * p.kv_total) * (int64_t)SLOT,
+                         tile_bytes, fb, policy);
+            }
           }
         } else {
           // one row (token) per lane
@@ -893,17 +902,24 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     for (int i = 0; i < 4; ++i) sacc[0][0][i] = at ? sacc[1][0][i] : sacc[0][0][i];
   }
 
-  // ---- per-token rulers (k_min, k_step | v_min, v_step) are read from shared
-  // memory where they are used, to keep registers free ----
+  // ---- per-token rulers (k_min, k_step | v_min, v_step) ----
+  auto tile = [&](int a) { return PK ? at : a; };
+  // one 8-byte read per token row: (k_min, k_step, v_min, v_step)
+  uint2 rr[NA][2];
+  if (LAYOUT != LAYOUT_PER_CHANNEL) {
+#pragma unroll
+    for (int a = 0; a < NA; ++a)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) rr[a][h] = *reinterpret_cast<const uint2*>(rrow + tile(a) * SV::r16 + h * SV::r8);
+  }
   auto ruler_k = [&](int a, int h) -> float2 {
     if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(p.use_quant ? -1.f : 0.f, 1.f);
-    return __half22float2(*reinterpret_cast<const __half2*>(rrow + a * SV::r16 + h * SV::r8));
+    return __half22float2(*reinterpret_cast<const __half2*>(&rr[PK ? 0 : a][h].x));
   };
   auto ruler_v = [&](int a, int h) -> float2 {
     if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(0.f, 1.f);
-    return __half22float2(*reinterpret_cast<const __half2*>(rrow + a * SV::r16 + h * SV::r8 + 4));
+    return __half22float2(*reinterpret_cast<const __half2*>(&rr[PK ? 0 : a][h].y));
   };
-  auto tile = [&](int a) { return PK ? at : a; };
   bool val[NA][2];
 #pragma unroll
   for (int a = 0; a < NA; ++a)

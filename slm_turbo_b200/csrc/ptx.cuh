@@ -119,6 +119,16 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// Tiled 2-D TMA copy global -> shared of the box at (c0, c1) of `tmap`, with
+// the same rules as tma_load_3d.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // L2 policy for data streamed once (the packed cache).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t p;

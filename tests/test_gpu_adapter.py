@@ -117,9 +117,15 @@ def _run(impl, st, dev):
     return out.float().view(-1, HQ, D).cpu().numpy()
 
 
-def test_mixed_batch_continuation_decode_and_fresh_prompt():
+@pytest.mark.parametrize("capture_path", [False, True])
+def test_mixed_batch_continuation_decode_and_fresh_prompt(capture_path, monkeypatch):
+    """Eager steps read the step's request offsets on the host; under CUDA
+    graph capture the impl takes an all-device path instead.  Both give the
+    oracle's answer (the capture path is selected here without a capture)."""
     ad, impl = _impl()
     from slm_turbo_b200.kernels import kv_dequant as kd
+    if capture_path:
+        monkeypatch.setattr(ad, "_capturing", lambda: True)
     dev = torch.device("cuda", torch.cuda.current_device())
     # continuation chunk of 40 over 300 cached, a decode row over 1000, a
     # fresh 25-token prompt, another continuation crossing page boundaries
@@ -136,8 +142,9 @@ def test_two_fresh_prompts_do_not_attend_across_requests():
     assert_close(_run(impl, st, dev), _expected(st), what="fresh prompts")
 
 
-def test_long_fresh_prompt_spans_several_row_blocks():
+def test_long_fresh_prompt_spans_several_row_blocks(monkeypatch):
     ad, impl = _impl()
+    monkeypatch.setattr(ad, "_capturing", lambda: True)  # the masked, row-blocked path
     dev = torch.device("cuda", torch.cuda.current_device())
     st = _step([(0, ad._PREFILL_ROWS + 300), (0, 7)], seed=6)
     assert_close(_run(impl, st, dev), _expected(st), what="long prompt")
