@@ -742,6 +742,85 @@ def run_c2(args):
     return 0
 
 
+def run_prefill(args):
+    """Row a6 / the tensor-core prefill kernel: per-channel prefill attention
+    (kv_dequant_prefill_attention) of M = S = 4096 query rows over the packed
+    keys/values, Hq32/Hkv8, D = --head-dim, causal.  The reference's own CUDA
+    prefill kernel (oracle/_ref, unmodified) runs on the same inputs on the
+    same GPU for the comparison and for an output cross-check.  Two rotating
+    input sets (q + out > L2 each).  One step = one prefill launch; ranks run
+    independent replicas."""
+    world, rank, dev, pg = _dist_setup()
+    from slm_turbo_b200.kernels import kv_dequant as kd
+    H, KV, M, S, Dh, NSETS = 32, 8, 4096, 4096, args.head_dim, 2
+    g = torch.Generator(device=dev).manual_seed(SEED + 40 + rank)
+    sets = []
+    for _ in range(NSETS):
+        k = torch.randn(KV, S, Dh, device=dev, generator=g).half()
+        v = torch.randn(KV, S, Dh, device=dev, generator=g).half()
+        kp, ks, kz = kd.kv_quantize_per_channel(k)
+        vp, vs, vz = kd.kv_quantize_per_channel(v)
+        q = torch.randn(H, M, Dh, device=dev, generator=g).half()
+        sets.append((q, kp, ks, kz, vp, vs, vz))
+        del k, v
+    torch.cuda.synchronize(dev)
+
+    def step(i):
+        kd.kv_dequant_prefill_attention(*sets[i], causal=True, num_kv_heads=KV)
+
+    steps = min(args.steps, 50)
+    ms, clocks, eager_ms = _timed(dev, pg, step, steps, args.warmup, NSETS)
+    assert kd.read_device_errors(dev) == 0
+    keys = sum(min(S, m + 1) for m in range(M))
+    flops = 4 * Dh * H * keys  # QK^T and PV, 2 flops per multiply-add
+    mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(mp.get("bf16_tflops", 1590.0))
+    peak_src = "MEASURED_PEAKS.json bf16_tflops (of measured)" if mp else "profiling-recipe fallback (of fallback)"
+    achieved = flops / (ms * 1e-3) / 1e12
+    ref_line = {"unavailable": "reference extension not built into oracle/_ref"}
+    try:
+        from oracle.build_ref import load_ref
+        ref = load_ref()
+        if ref is not None and rank == 0:
+            ours = kd.kv_dequant_prefill_attention(*sets[0], causal=True, num_kv_heads=KV)
+            theirs = ref.kv_dequant_prefill_attention_cuda(*sets[0], 16, 64 if Dh == 64 else 32, True, True, KV)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(3):
+                ref.kv_dequant_prefill_attention_cuda(*sets[i % NSETS], 16, 64 if Dh == 64 else 32, True, True, KV)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            rms = e0.elapsed_time(e1) / 3
+            ref_line = {"ms_per_step": rms, "tflops": flops / (rms * 1e-3) / 1e12, "speedup_ours": rms / ms,
+                        "max_abs_diff_vs_ours": float((ours - theirs).abs().max()),
+                        "mode": "reference kv_dequant_prefill_attention_cuda (built unmodified, sm_100a), "
+                                "3 launches between CUDA events, same inputs"}
+    except Exception as exc:  # the comparison is informative, never the measured line
+        ref_line = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    if pg is not None:
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    print(json.dumps({
+        "metric": "prefill rows/s (per-channel 4-bit prefill attention)", "value": M * world / (ms * 1e-3),
+        "unit": "rows/s", "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms,
+        "eager_ms_per_step": eager_ms,
+        "step_issue": "steps replayed from CUDA graphs of the captured public-API calls; eager_ms_per_step: "
+                      "the same steps issued from Python",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"prefill (row a6): H32/KV8/D{Dh}, M=S=4096, causal, per-channel rulers",
+                   "l2": f"{NSETS} rotating input sets (q 32 MB + out 64 MB each)",
+                   "parallelism": f"replicas x{world} (no collective)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "kernel": f"prefill_pc_kernel<{Dh}>",
+                     "algorithmic_flops_per_launch": flops, "peak_source": peak_src,
+                     "note": "mma.sync m16n8k16 tiles; the peak is cuBLAS bf16 on tcgen05"},
+        "reference_cuda_same_box": ref_line,
+        "e2e": None, "gpu_launches": steps, "clocks": clocks, "cpu_baseline": None}), flush=True)
+    return 0
+
+
 def run_c4(args):
     """long-context decode, 4 sequences of 131,072 tokens,
     Hq64/Hkv8/D128, paged per-token 4-bit, block 16; split-K over the
@@ -838,7 +917,10 @@ if mode == "refkern":
     Impl.do_kv_cache_update = store
     Impl._decode_attention = decode
 from vllm import LLM, SamplingParams
-kw = dict(model=model_dir, load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
+# the reference's store and decode kernels accept fp16 only
+# (kernels/kv_dequant_cuda.cu:359-360, 419-420): its arm runs the model in fp16
+kw = dict(model=model_dir, load_format="dummy", skip_tokenizer_init=True,
+          dtype="float16" if mode == "refkern" else "bfloat16",
           attention_backend="CUSTOM", block_size=16, max_model_len=lmax + steps + 32, max_num_seqs=n_seqs,
           max_num_batched_tokens=16384, gpu_memory_utilization=0.6, enable_prefix_caching=False, seed=0)
 if mode == "ours-graph":
@@ -920,8 +1002,9 @@ def run_reference_c5(args):
     v = r.get("decode_tok_s")
     print(json.dumps({"metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": world,
                       "steps": C5_REF_STEPS, "warmup": 1, "higher_is_better": True, "scaling": "weak",
-                      "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                      "config": {"workload": "C5 (see the ours line); reference CUDA kernels, per-request loop"},
+                      "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                      "config": {"workload": "C5 (see the ours line); reference CUDA kernels, per-request loop; "
+                                             "model in fp16 (the reference kernels reject bf16)"},
                       "engine": r}), flush=True)
     return 0
 
@@ -974,9 +1057,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="c3", choices=["c3", "c2", "c4", "c5"],
-                    help="c3 (default, the metric's config); c2 / c4 / c5 print extra lines")
-    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128], help="c2 only")
+    ap.add_argument("--workload", default="c3", choices=["c3", "c2", "c4", "c5", "prefill"],
+                    help="c3 (default, the metric's config); c2 / c4 / c5 / prefill print extra lines")
+    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 80, 128], help="c2 and prefill only")
     args = ap.parse_args()
     if args.impl == "reference" and args.workload == "c5":
         return run_reference_c5(args)
@@ -988,6 +1071,8 @@ def main():
         return run_c4(args)
     if args.workload == "c5":
         return run_c5(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
     return run_ours(args)
 
 

@@ -239,8 +239,11 @@ int slmt_per_token_decode(
  * Per-channel prefill attention: q [num_q_heads, M, head_dim] against one
  * per-channel K/V of S tokens ([KV, S, D/2] codes, [KV, D] rulers).  causal!=0
  * lets query row m see keys 0..m (ref mask `m_idx >= n_abs`).  out
- * [num_q_heads, M, head_dim] in out_dtype.  Workspace from
- * slmt_decode_workspace_bytes(M, ...).
+ * [num_q_heads, M, head_dim] in out_dtype.  M-tiled kernel (64 query rows
+ * per CTA over 64-token K/V chunks dequantized once in shared memory);
+ * workspace and err_flag are accepted and unused (may be NULL).  Codes must
+ * be 4-byte aligned.  With seq_len 0 every row is zero and codes/rulers may
+ * be NULL.
  * ref: kv_dequant_prefill_attention_cuda, kernels/kv_dequant_cuda.cu:182-272
  *      (kernel .cuh:293-502; Python kernels/kv_dequant.py:129-177).
  */
@@ -252,6 +255,35 @@ int slmt_per_channel_prefill(
     int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
     float sm_scale, void* out, int out_dtype, int64_t out_head_stride,
     int64_t out_row_stride, void* workspace, int64_t workspace_bytes,
+    int32_t* err_flag, void* stream);
+
+/*
+ * Prefill attention of query chunks over the paged per-token cache (the
+ * layout of slmt_paged_decode).  Request r (r < num_reqs) owns query rows
+ * [query_start_loc[r], query_start_loc[r+1]) of q (row m, head h at
+ * q + m*q_row_stride + h*q_head_stride); those n rows are the LAST n of its
+ * seq_lens[r] cached tokens (the step's new tokens already stored), so row i
+ * attends causally to keys [0, seq_lens[r] - n + i + 1) read through
+ * block_tables.  max_query_len bounds n: the launch covers 64-row tiles up
+ * to max_query_len, and a request with rows beyond them sets
+ * SLMT_DEVERR_SEQ_LEN and those rows are not written.  out like q, in
+ * out_dtype.  Bad block-table entries set SLMT_DEVERR_BLOCK_ID (the token
+ * reads as zero), lengths above max_blocks_per_seq*block_size set
+ * SLMT_DEVERR_SEQ_LEN (clamped).  No workspace, no host sync.  kv_cache must
+ * be 8-byte aligned; num_reqs and num_q_heads at most 65535.
+ * Replaces the reference adapter's prefill branch, which runs SDPA over the
+ * step's raw K/V only (adapters/vllm_adapter.py:218-243), for chunks with a
+ * cached prefix; same M-tiled kernel as slmt_per_channel_prefill
+ * (ref kernel .cuh:293-502).
+ */
+int slmt_paged_prefill(
+    const void* q, int q_dtype, int64_t q_row_stride, int64_t q_head_stride,
+    const uint8_t* kv_cache, int64_t num_blocks, int64_t block_size,
+    int64_t num_kv_heads, int64_t head_dim, const void* block_tables,
+    int bt_dtype, int64_t bt_seq_stride, int64_t max_blocks_per_seq,
+    const int32_t* query_start_loc, const int32_t* seq_lens, int64_t num_reqs,
+    int64_t max_query_len, int64_t num_q_heads, float sm_scale, void* out,
+    int out_dtype, int64_t out_row_stride, int64_t out_head_stride,
     int32_t* err_flag, void* stream);
 
 /*

@@ -171,7 +171,7 @@ def pc_decode(q, k_packed, k_scale, k_zero, v_packed, v_scale, v_zero, *, use_qu
 
 
 def pc_prefill(q, k_packed, k_scale, k_zero, v_packed, v_scale, v_zero, *, causal=True,
-               use_quant=True, sm_scale=None, nthreads=None):
+               use_quant=True, bf16=False, sm_scale=None, nthreads=None):
     """Per-channel prefill. q [H, M, D]; codes [KV, S, D/2]; rulers [KV, D] -> [H, M, D]."""
     qb = _u16(q)
     hq, m, d = qb.shape
@@ -180,7 +180,7 @@ def pc_prefill(q, k_packed, k_scale, k_zero, v_packed, v_scale, v_zero, *, causa
     rs = [_u16(t) for t in (k_scale, k_zero, v_scale, v_zero)]
     out = np.empty((hq, m, d), np.float32)
     scale = (1.0 / np.sqrt(d)) if sm_scale is None else float(sm_scale)
-    lib().oracle_pc_decode(_p(qb), 0, d, m * d, _p(kp), _p(vp), 0, s, *[_p(r) for r in rs], 0,
+    lib().oracle_pc_decode(_p(qb), int(bf16), d, m * d, _p(kp), _p(vp), 0, s, *[_p(r) for r in rs], 0,
                            int(use_quant), None, s, int(causal), m, hq, kv, d, scale, _p(out), d, m * d,
                            nthreads or nthreads_default())
     return out

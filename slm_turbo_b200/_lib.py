@@ -47,6 +47,8 @@ SIGNATURES = {
     "slmt_per_channel_prefill": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _i32,
                                         _i64, _i64, _i64, _i64, _f32, _vp, _i32, _i64, _i64, _vp, _i64, _vp,
                                         _vp]),
+    "slmt_paged_prefill": (_i32, [_vp, _i32, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _i32, _i64, _i64,
+                                  _vp, _vp, _i64, _i64, _i64, _f32, _vp, _i32, _i64, _i64, _vp, _vp]),
     "slmt_per_channel_quantize": (_i32, [_vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
     "slmt_per_channel_append": (_i32, [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64,
                                        _vp]),

@@ -180,10 +180,12 @@ def _register_custom_backend() -> bool:
                 from slm_turbo_b200.kernels.kv_dequant import (
                     _load_cuda_extension,
                     kv_decode_paged_batched,
+                    kv_prefill_paged,
                     kv_quantize_store,
                 )
                 _load_cuda_extension()
                 self._slm_decode_batched = kv_decode_paged_batched
+                self._slm_prefill = kv_prefill_paged
                 self._slm_store = kv_quantize_store
                 self._slm_kernel = torch.cuda.is_available()
                 if not self._slm_kernel:
@@ -193,6 +195,7 @@ def _register_custom_backend() -> bool:
             if self._slm_kernel_err:
                 logger.warning("slm-turbo kernel disabled in this process: %s", self._slm_kernel_err)
                 self._slm_decode_batched = self._kernel_unavailable
+                self._slm_prefill = self._kernel_unavailable
                 self._slm_store = self._kernel_unavailable
 
         def _kernel_unavailable(self, *args, **kwargs):
@@ -234,48 +237,44 @@ def _register_custom_backend() -> bool:
 
         def _prefill_attention(self, query, key, value, kv_cache, attn_metadata, out):
             """Per request: raw-K/V causal attention for a request with no cached
-            context (the reference's first-chunk SDPA, :230-243), the packed
-            cache through the block table for every other query token."""
+            context (the reference's first-chunk SDPA, :230-243); every other
+            request's query rows attend to its packed cache through the block
+            table, all such requests in one M-tiled prefill launch."""
             if _capturing():
                 return self._prefill_attention_device(query, key, value, kv_cache, attn_metadata, out)
             global _KERNEL_CALLS
             n, hq, d = query.shape
             nreq = attn_metadata.seq_lens.shape[0]
             # one host read of the step's request offsets (eager steps only;
-            # under graph capture the all-device path above runs)
-            qsl = attn_metadata.query_start_loc[:nreq + 1].tolist()
+            # under graph capture the all-device path below runs)
+            qsl = [min(x, n) for x in attn_metadata.query_start_loc[:nreq + 1].tolist()]
             seq_lens = attn_metadata.seq_lens[:nreq].tolist()
-            cached_rows, cached_lens, cached_req = [], [], []
             hk = key.shape[1]
+            kernel_lens, longest = [], 0
             for r in range(nreq):
-                a, b = qsl[r], min(qsl[r + 1], n)
-                if b <= a:
-                    continue
-                ctx = seq_lens[r] - (qsl[r + 1] - qsl[r])
-                if ctx <= 0:  # all of this request's tokens are new: causal over them
+                a, b = qsl[r], qsl[r + 1]
+                ctx = seq_lens[r] - (b - a)
+                if b > a and ctx > 0:  # rows a..b-1 are the last b-a of seq_lens[r] cached tokens
+                    kernel_lens.append(seq_lens[r])
+                    longest = max(longest, b - a)
+                else:  # nothing cached before this chunk (or no rows): the kernel skips it
+                    kernel_lens.append(0)
+            if longest:
+                dev = query.device
+                self._slm_prefill(
+                    query, kv_cache, attn_metadata.block_table[:nreq],
+                    torch.tensor(qsl, dtype=torch.int32).to(dev, non_blocking=True),
+                    torch.tensor(kernel_lens, dtype=torch.int32).to(dev, non_blocking=True), longest,
+                    block_size=kv_cache.shape[1], num_kv_heads=kv_cache.shape[2], out=out, sm_scale=self.scale)
+                _KERNEL_CALLS += 1
+            for r in range(nreq):
+                a, b = qsl[r], qsl[r + 1]
+                if b > a and kernel_lens[r] == 0:  # all of this request's tokens are new: causal over them
                     o = torch.nn.functional.scaled_dot_product_attention(
                         query[a:b].transpose(0, 1).unsqueeze(0), key[a:b].transpose(0, 1).unsqueeze(0),
                         value[a:b].transpose(0, 1).unsqueeze(0), is_causal=True, scale=self.scale,
                         enable_gqa=hk < hq)
                     out[a:b] = o[0].transpose(0, 1).to(out.dtype)
-                else:  # token j attends to positions 0..ctx+j of the packed cache
-                    cached_rows.append((a, b))
-                    cached_lens.append((ctx + 1, ctx + 1 + (b - a)))
-                    cached_req.append(r)
-            if cached_rows:
-                dev = query.device
-                rows = torch.cat([torch.arange(a, b) for a, b in cached_rows]).to(dev)
-                lens = torch.cat([torch.arange(l0, l1, dtype=torch.int32) for l0, l1 in cached_lens]).to(dev)
-                reqs = torch.cat([torch.full((b - a,), r, dtype=torch.long)
-                                  for (a, b), r in zip(cached_rows, cached_req)]).to(dev)
-                bt = attn_metadata.block_table[:nreq].index_select(0, reqs)
-                sub = torch.empty(rows.numel(), hq, d, dtype=out.dtype, device=dev)
-                self._slm_decode_batched(
-                    query.index_select(0, rows), kv_cache, bt, lens, block_size=kv_cache.shape[1],
-                    num_kv_heads=kv_cache.shape[2], out=sub, sm_scale=self.scale,
-                    max_seq_len=max(l1 for _, l1 in cached_lens) - 1)
-                out.index_copy_(0, rows, sub)
-                _KERNEL_CALLS += 1
             return out
 
         def _prefill_attention_device(self, query, key, value, kv_cache, attn_metadata, out):

@@ -23,7 +23,7 @@ LIB_NAME = "libslm_turbo_b200.so"
 LIB_PATH = HERE / LIB_NAME
 SOURCES = ["decode.cu", "store.cu", "decode_noalloc.cu",
            "decode_d64_paged.cu", "decode_d64_contig.cu", "decode_d80_paged.cu", "decode_d80_contig.cu",
-           "decode_d128_paged.cu", "decode_d128_contig.cu"]
+           "decode_d128_paged.cu", "decode_d128_contig.cu", "prefill.cu"]
 HEADERS = ["ptx.cuh", "decode_common.cuh", "decode_kernels.cuh", "decode_dispatch.cuh", "quant_store.cuh",
            "internal.h"]
 

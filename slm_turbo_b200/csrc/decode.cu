@@ -608,12 +608,63 @@ extern "C" int slmt_per_channel_prefill(
     int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, float sm_scale,
     void* out, int out_dtype, int64_t out_head_stride, int64_t out_row_stride,
     void* workspace, int64_t workspace_bytes, int32_t* err_flag, void* stream) {
-  // Query row m is a pseudo-sequence of length (causal ? min(S, m+1) : S)
-  // over the one shared K/V (sequence stride 0).
-  if (seq_len < 0 || num_rows < 0) return SLMT_ERR_SHAPE;
-  return contig_decode(LAYOUT_PER_CHANNEL, q, q_dtype, q_row_stride, q_head_stride, k_packed,
-                       v_packed, 0, seq_len, k_scale, k_zero, v_scale, v_zero, 0, use_quant,
-                       nullptr, seq_len, causal ? 1 : 0, num_rows, num_q_heads, num_kv_heads,
-                       head_dim, sm_scale, out, out_dtype, out_row_stride, out_head_stride,
-                       workspace, workspace_bytes, err_flag, stream);
+  // M-tiled kernel (prefill.cu): needs no split-K workspace and sets no error
+  // bits (every read is bounded by seq_len); both arguments are accepted for
+  // the signature's sake.
+  (void)workspace;
+  (void)workspace_bytes;
+  (void)err_flag;
+  if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
+  if (seq_len < 0 || num_rows < 0 || seq_len > INT32_MAX / 2 || num_rows > INT32_MAX / 2) return SLMT_ERR_SHAPE;
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0) return SLMT_ERR_SHAPE;
+  if (num_q_heads > 65535) return SLMT_ERR_UNSUPPORTED;
+  if (num_rows == 0) return SLMT_OK;
+  if (!q || !out) return SLMT_ERR_NULL;
+  // with no keys (seq_len 0) every row is zero and codes/rulers are not read
+  if (seq_len > 0 && (!k_packed || !v_packed)) return SLMT_ERR_NULL;
+  if (seq_len > 0 && use_quant && (!k_scale || !k_zero || !v_scale || !v_zero)) return SLMT_ERR_NULL;
+  if (q_dtype != SLMT_DTYPE_F16 && q_dtype != SLMT_DTYPE_BF16) return SLMT_ERR_DTYPE;
+  if (out_dtype != SLMT_DTYPE_F32 && out_dtype != SLMT_DTYPE_F16 && out_dtype != SLMT_DTYPE_BF16)
+    return SLMT_ERR_DTYPE;
+  // codes are read as 4-byte words, q two elements at a time
+  if (reinterpret_cast<uintptr_t>(k_packed) % 4 != 0 || reinterpret_cast<uintptr_t>(v_packed) % 4 != 0 ||
+      reinterpret_cast<uintptr_t>(q) % 2 != 0)
+    return SLMT_ERR_ALIGN;
+  return prefill_pc_launch(q, q_dtype == SLMT_DTYPE_BF16, q_head_stride, q_row_stride, k_packed, v_packed,
+                           seq_len, k_scale, k_zero, v_scale, v_zero, use_quant, causal, num_rows, num_q_heads,
+                           num_kv_heads, head_dim, sm_scale, out, out_dtype_code(out_dtype), out_head_stride,
+                           out_row_stride, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int slmt_paged_prefill(
+    const void* q, int q_dtype, int64_t q_row_stride, int64_t q_head_stride,
+    const uint8_t* kv_cache, int64_t num_blocks, int64_t block_size,
+    int64_t num_kv_heads, int64_t head_dim, const void* block_tables,
+    int bt_dtype, int64_t bt_seq_stride, int64_t max_blocks_per_seq,
+    const int32_t* query_start_loc, const int32_t* seq_lens, int64_t num_reqs,
+    int64_t max_query_len, int64_t num_q_heads, float sm_scale, void* out,
+    int out_dtype, int64_t out_row_stride, int64_t out_head_stride,
+    int32_t* err_flag, void* stream) {
+  if (!valid_head_dim(head_dim)) return SLMT_ERR_HEAD_DIM;
+  if (num_reqs < 0 || max_query_len < 0 || num_blocks < 0 || block_size <= 0 || max_blocks_per_seq < 0)
+    return SLMT_ERR_SHAPE;
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0) return SLMT_ERR_SHAPE;
+  if (num_q_heads > 65535 || num_reqs > 65535) return SLMT_ERR_UNSUPPORTED;
+  if (max_query_len > INT32_MAX / 2) return SLMT_ERR_SHAPE;
+  if (num_reqs == 0 || max_query_len == 0) return SLMT_OK;
+  if (!q || !out || !kv_cache || !block_tables || !query_start_loc || !seq_lens) return SLMT_ERR_NULL;
+  if (q_dtype != SLMT_DTYPE_F16 && q_dtype != SLMT_DTYPE_BF16) return SLMT_ERR_DTYPE;
+  if (out_dtype != SLMT_DTYPE_F32 && out_dtype != SLMT_DTYPE_F16 && out_dtype != SLMT_DTYPE_BF16)
+    return SLMT_ERR_DTYPE;
+  if (bt_dtype != SLMT_DTYPE_I32 && bt_dtype != SLMT_DTYPE_I64) return SLMT_ERR_DTYPE;
+  if (num_reqs > 1 && bt_seq_stride < max_blocks_per_seq) return SLMT_ERR_SHAPE;
+  if (max_blocks_per_seq * block_size > INT32_MAX / 2) return SLMT_ERR_SHAPE;
+  // slot rows are read as 4-byte code words and one 8-byte ruler quad
+  if (reinterpret_cast<uintptr_t>(kv_cache) % 8 != 0 || reinterpret_cast<uintptr_t>(q) % 2 != 0)
+    return SLMT_ERR_ALIGN;
+  return prefill_paged_launch(q, q_dtype == SLMT_DTYPE_BF16, q_row_stride, q_head_stride, kv_cache, num_blocks,
+                              block_size, num_kv_heads, head_dim, block_tables, bt_dtype == SLMT_DTYPE_I64,
+                              bt_seq_stride, max_blocks_per_seq, query_start_loc, seq_lens, num_reqs, max_query_len,
+                              num_q_heads, sm_scale, out, out_dtype_code(out_dtype), out_row_stride, out_head_stride,
+                              err_flag, reinterpret_cast<cudaStream_t>(stream));
 }

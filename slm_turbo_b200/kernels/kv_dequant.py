@@ -180,13 +180,13 @@ def kv_dequant_prefill_attention(
     ks, kz, vs, vz = (t.contiguous() for t in (k_scale, k_zero, v_scale, v_zero))
     out = torch.empty(H, M, D, dtype=torch.float32, device=q.device)
     dev = q.device
-    ws = _lib.workspace(dev, M, H, num_kv_heads, D)
+    # the M-tiled prefill kernel keeps no split-K partials: no workspace
     rc = L.slmt_per_channel_prefill(
         _lib.ptr(q), _lib.dtype_tag(q.dtype), q.stride(0), q.stride(1),
         _lib.ptr(kp), _lib.ptr(vp), S, _lib.ptr(ks), _lib.ptr(kz), _lib.ptr(vs), _lib.ptr(vz),
         int(bool(use_quant)), int(bool(causal)), M, H, num_kv_heads, D, float(1.0 / math.sqrt(D)),
         _lib.ptr(out), _lib.DT_F32, out.stride(0), out.stride(1),
-        _lib.ptr(ws), ws.numel(), _lib.ptr(_lib.error_word(dev)), _lib.stream_of(dev))
+        None, 0, _lib.ptr(_lib.error_word(dev)), _lib.stream_of(dev))
     _lib.check(rc, "kv_dequant_prefill")
     return out
 
@@ -368,6 +368,53 @@ def kv_append_decode_paged_batched(q, new_key, new_value, kv_cache, block_tables
         _lib.ptr(out), _lib.dtype_tag(out.dtype), out.stride(0), out.stride(1),
         _lib.ptr(ws), ws.numel(), _lib.ptr(_lib.error_word(dev)), _lib.stream_of(dev))
     _lib.check(rc, "append-decode")
+    return out
+
+
+def kv_prefill_paged(q, kv_cache, block_tables, query_start_loc, seq_lens, max_query_len, block_size=None,
+                     num_kv_heads=None, out=None, sm_scale=None):
+    """Prefill attention of query chunks over the paged packed cache, one
+    M-tiled launch for all requests.
+
+    q [N, Hq, D] (fp16/bf16, unit head-dim stride): request r owns rows
+    query_start_loc[r] .. query_start_loc[r+1]-1, the LAST of its
+    seq_lens[r] tokens, which must already be stored in kv_cache [NB, bs, KV,
+    D+8]; row i attends causally to keys [0, seq_lens[r] - n_r + i + 1)
+    through block_tables [R, max_blocks] (int32/int64).  query_start_loc
+    [R+1] and seq_lens [R] int32 on the device; max_query_len (host int)
+    bounds n_r.  Returns out [N, Hq, D] (fp32 by default, or the given
+    ``out``).  Replaces the reference adapter's raw-K/V SDPA prefill for
+    chunks with a cached prefix (adapters/vllm_adapter.py:218-243).
+    """
+    L = _lib.load()
+    N, H, D = q.shape
+    bs = kv_cache.size(1) if block_size is None else int(block_size)
+    kv = kv_cache.size(2) if num_kv_heads is None else int(num_kv_heads)
+    _require_cuda(q, "paged prefill: q", _QDT)
+    if kv_cache.dtype != torch.uint8 or not kv_cache.is_contiguous():
+        raise RuntimeError("paged prefill: kv_cache must be contiguous uint8")
+    if q.stride(2) != 1:
+        q = q.contiguous()
+    if out is None:
+        out = torch.empty(N, H, D, dtype=torch.float32, device=q.device)
+    qsl = query_start_loc if (query_start_loc.dtype == torch.int32 and query_start_loc.is_contiguous()) \
+        else query_start_loc.to(torch.int32).contiguous()
+    sl = seq_lens if (seq_lens.dtype == torch.int32 and seq_lens.is_contiguous()) \
+        else seq_lens.to(torch.int32).contiguous()
+    R = sl.numel()
+    if qsl.numel() < R + 1:
+        raise RuntimeError(f"paged prefill: query_start_loc needs {R + 1} entries, has {qsl.numel()}")
+    bt = block_tables if block_tables.stride(-1) == 1 else block_tables.contiguous()
+    dev = q.device
+    rc = L.slmt_paged_prefill(
+        _lib.ptr(q), _lib.dtype_tag(q.dtype), q.stride(0), q.stride(1),
+        _lib.ptr(kv_cache), kv_cache.size(0), bs, kv, D,
+        _lib.ptr(bt), _lib.dtype_tag(bt.dtype), bt.stride(0), bt.size(-1),
+        _lib.ptr(qsl), _lib.ptr(sl), R, int(max_query_len), H,
+        float(1.0 / math.sqrt(D) if sm_scale is None else sm_scale),
+        _lib.ptr(out), _lib.dtype_tag(out.dtype), out.stride(0), out.stride(1),
+        _lib.ptr(_lib.error_word(dev)), _lib.stream_of(dev))
+    _lib.check(rc, "paged prefill")
     return out
 
 

@@ -32,6 +32,7 @@ def _impl():
     impl.num_heads, impl.head_size, impl.num_kv_heads, impl.scale = HQ, D, KV, D ** -0.5
     impl._slm_kernel, impl._slm_kernel_err, impl._slm_meta = True, None, None
     impl._slm_decode_batched, impl._slm_store = kd.kv_decode_paged_batched, kd.kv_quantize_store
+    impl._slm_prefill = kd.kv_prefill_paged
     return ad, impl
 
 

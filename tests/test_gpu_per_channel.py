@@ -125,6 +125,55 @@ def test_prefill_vs_golden_and_oracle(causal):
         assert_close(out.cpu().numpy(), z[f"{name}/out"], what="prefill vs reference golden")
 
 
+# M-tiled prefill kernel: row tiles of 64 over 64-token K/V chunks, so the
+# cases straddle both tile sizes, put M above and below S (rows past S attend
+# to all S keys when causal), share kv heads across q heads and cover every
+# head size, bf16 q and the unquantized mode.
+PREFILL_CASES = [
+    # (H, KV, M, S, D, causal, q dtype, use_quant)
+    (8, 2, 200, 200, 64, True, torch.float16, True),
+    (8, 8, 130, 77, 64, True, torch.float16, True),
+    (4, 1, 65, 300, 80, False, torch.bfloat16, True),
+    (6, 2, 257, 129, 80, True, torch.float16, True),
+    (8, 2, 512, 512, 128, True, torch.bfloat16, True),
+    (4, 4, 100, 1000, 128, False, torch.float16, True),
+    (2, 1, 64, 64, 128, True, torch.float16, False),
+    (3, 1, 1, 5, 64, True, torch.float16, True),
+]
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES, ids=lambda c: "h{}_kv{}_m{}_s{}_d{}_{}_{}_{}".format(
+    c[0], c[1], c[2], c[3], c[4], "causal" if c[5] else "full", str(c[6])[6:], "q" if c[7] else "raw"))
+def test_prefill_tiles_vs_oracle(case):
+    kd = _kd()
+    h, kv, m, s, d, causal, qdt, use_quant = case
+    g = torch.Generator().manual_seed(h * 1000 + m + s + d)
+    q = torch.randn(h, m, d, generator=g).to(qdt)
+    k = torch.randn(kv, s, d, generator=g).half()
+    v = torch.randn(kv, s, d, generator=g).half()
+    dev = torch.device("cuda")
+    kp, ks, kz = kd.kv_quantize_per_channel(k.to(dev))
+    vp, vs, vz = kd.kv_quantize_per_channel(v.to(dev))
+    if not use_quant:  # raw codes as values: scale the query so the softmax stays soft
+        q = (q.float() / 16).to(qdt)
+    out = kd.kv_dequant_prefill_attention(q.to(dev), kp, ks, kz, vp, vs, vz, causal=causal,
+                                          use_quant=use_quant, num_kv_heads=kv)
+    want = oracle.pc_prefill(q, kp.cpu(), ks.cpu(), kz.cpu(), vp.cpu(), vs.cpu(), vz.cpu(),
+                             causal=causal, use_quant=use_quant, bf16=qdt == torch.bfloat16)
+    scale = 16.0 if not use_quant else 1.0  # raw codes are values in [0, 15]
+    assert_close(out.cpu().numpy() / scale, want / scale, what="m-tiled prefill vs oracle")
+
+
+def test_prefill_empty_kv_gives_zero_rows():
+    kd = _kd()
+    dev = torch.device("cuda")
+    q = torch.randn(4, 10, 64, device=dev).half()
+    kp = torch.zeros(2, 0, 32, dtype=torch.uint8, device=dev)
+    r = torch.ones(2, 64, dtype=torch.float16, device=dev)
+    out = kd.kv_dequant_prefill_attention(q, kp, r, r, kp, r, r, num_kv_heads=2)
+    assert out.shape == (4, 10, 64) and torch.count_nonzero(out).item() == 0
+
+
 def test_per_token_contiguous_decode():
     kd = _kd()
     dev = torch.device("cuda")
