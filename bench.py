@@ -1049,6 +1049,48 @@ def run_c5(args):
     return 0
 
 
+def run_ncu_case(args):
+    """A few untimed launches of one kernel on a bench workload, for an ncu
+    capture (`-k regex:... -s 2 -c 1`): `decode` / `fused` = the C3 decode
+    (plain, or with the step's append) on rank 0's pool, `prefill` = the
+    per-channel prefill of `--workload prefill` (D = --head-dim).  Five
+    launches, then a device-error check; nothing is timed or printed but a
+    status line."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from slm_turbo_b200.kernels import kv_dequant as kd
+    if args.ncu_case == "prefill":
+        H, KV, M, S, Dh = 32, 8, 4096, 4096, args.head_dim
+        g = torch.Generator(device=dev).manual_seed(SEED + 40)
+        k = torch.randn(KV, S, Dh, device=dev, generator=g).half()
+        v = torch.randn(KV, S, Dh, device=dev, generator=g).half()
+        kp, ks, kz = kd.kv_quantize_per_channel(k)
+        vp, vs, vz = kd.kv_quantize_per_channel(v)
+        q = torch.randn(H, M, Dh, device=dev, generator=g).half()
+        for _ in range(5):
+            kd.kv_dequant_prefill_attention(q, kp, ks, kz, vp, vs, vz, causal=True, num_kv_heads=KV)
+    else:
+        w = build_workload(rank_lengths(1, 0), 0)
+        cache = prefill_cache(w, dev)
+        B = len(w["lengths"])
+        bt_d, sl_d = w["block_tables"].to(dev), w["seq_lens1"].to(dev)
+        g = torch.Generator(device=dev).manual_seed(SEED + 11)
+        q = torch.randn(B, HQ, D, device=dev, generator=g).half()
+        k_new = torch.randn(B, HKV, D, device=dev, generator=g).half()
+        v_new = torch.randn(B, HKV, D, device=dev, generator=g).half()
+        out = torch.empty(B, HQ, D, dtype=torch.float32, device=dev)
+        maxlen = int(w["seq_lens1"].max())
+        for _ in range(5):
+            if args.ncu_case == "fused":
+                kd.kv_append_decode_paged_batched(q, k_new, v_new, cache, bt_d, sl_d, out=out, max_seq_len=maxlen)
+            else:
+                kd.kv_decode_paged_batched(q, cache, bt_d, sl_d, out=out, max_seq_len=maxlen)
+    torch.cuda.synchronize(dev)
+    err = kd.read_device_errors(dev)
+    print(f"ncu case {args.ncu_case}: 5 launches, device errors {err}")
+    return 0 if err == 0 else 1
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1060,7 +1102,11 @@ def main():
     ap.add_argument("--workload", default="c3", choices=["c3", "c2", "c4", "c5", "prefill"],
                     help="c3 (default, the metric's config); c2 / c4 / c5 / prefill print extra lines")
     ap.add_argument("--head-dim", type=int, default=128, choices=[64, 80, 128], help="c2 and prefill only")
+    ap.add_argument("--ncu-case", choices=["decode", "fused", "prefill"], default=None,
+                    help="untimed launches of one kernel for an ncu capture (no JSON line)")
     args = ap.parse_args()
+    if args.ncu_case:
+        return run_ncu_case(args)
     if args.impl == "reference" and args.workload == "c5":
         return run_reference_c5(args)
     if args.impl == "reference":

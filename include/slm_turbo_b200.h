@@ -242,7 +242,7 @@ int slmt_per_token_decode(
  * [num_q_heads, M, head_dim] in out_dtype.  M-tiled kernel (64 query rows
  * per CTA over 64-token K/V chunks dequantized once in shared memory);
  * workspace and err_flag are accepted and unused (may be NULL).  Codes must
- * be 4-byte aligned.  With seq_len 0 every row is zero and codes/rulers may
+ * be 8-byte aligned.  With seq_len 0 every row is zero and codes/rulers may
  * be NULL.
  * ref: kv_dequant_prefill_attention_cuda, kernels/kv_dequant_cuda.cu:182-272
  *      (kernel .cuh:293-502; Python kernels/kv_dequant.py:129-177).
@@ -264,8 +264,10 @@ int slmt_per_channel_prefill(
  * q + m*q_row_stride + h*q_head_stride); those n rows are the LAST n of its
  * seq_lens[r] cached tokens (the step's new tokens already stored), so row i
  * attends causally to keys [0, seq_lens[r] - n + i + 1) read through
- * block_tables.  max_query_len bounds n: the launch covers 64-row tiles up
- * to max_query_len, and a request with rows beyond them sets
+ * block_tables.  A request with seq_lens[r] <= 0 is skipped (its rows of out
+ * are left as they are; a caller attends those rows some other way).
+ * max_query_len bounds n of the other requests: the launch covers 64-row
+ * tiles up to max_query_len, and a request with rows beyond them sets
  * SLMT_DEVERR_SEQ_LEN and those rows are not written.  out like q, in
  * out_dtype.  Bad block-table entries set SLMT_DEVERR_BLOCK_ID (the token
  * reads as zero), lengths above max_blocks_per_seq*block_size set

@@ -257,7 +257,7 @@ def _register_custom_backend() -> bool:
                 if b > a and ctx > 0:  # rows a..b-1 are the last b-a of seq_lens[r] cached tokens
                     kernel_lens.append(seq_lens[r])
                     longest = max(longest, b - a)
-                else:  # nothing cached before this chunk (or no rows): the kernel skips it
+                else:  # nothing cached before this chunk (or no rows): length 0, the kernel skips it
                     kernel_lens.append(0)
             if longest:
                 dev = query.device

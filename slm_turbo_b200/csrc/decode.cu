@@ -21,11 +21,12 @@ inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
 // One translation unit per (head dim, layout family) instantiates the
 // kernels and returns the one a call needs (decode_d*.cu); this file
 // instantiates none, so the library's sources compile in parallel.
-DecodeFn decode_fn(int D, int nt, bool pk, int layout, int kvc, bool append) {
+DecodeFn decode_fn(int D, int nt, bool pk, int layout, int kvc, bool append, bool swz) {
   const bool paged = layout == LAYOUT_PAGED;
-  if (D == 64) return paged ? decode_fn_64_paged(nt, pk, kvc, append) : decode_fn_64_contig(nt, pk, layout, kvc);
-  if (D == 80) return paged ? decode_fn_80_paged(nt, pk, kvc, append) : decode_fn_80_contig(nt, pk, layout, kvc);
-  return paged ? decode_fn_128_paged(nt, pk, kvc, append) : decode_fn_128_contig(nt, pk, layout, kvc);
+  if (D == 64)
+    return paged ? decode_fn_64_paged(nt, pk, kvc, append, swz) : decode_fn_64_contig(nt, pk, layout, kvc);
+  if (D == 80) return paged ? decode_fn_80_paged(nt, pk, kvc, append, false) : decode_fn_80_contig(nt, pk, layout, kvc);
+  return paged ? decode_fn_128_paged(nt, pk, kvc, append, swz) : decode_fn_128_contig(nt, pk, layout, kvc);
 }
 
 struct OccEntry {
@@ -144,6 +145,28 @@ bool encode_pool_map(CUtensorMap* m, const uint8_t* base, int64_t rows, int64_t 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Swizzled variant of the whole-row page-tile copy (paged mode 4): the pool
+// [rows][kv*(D+8) bytes] as 8-byte elements [rows][kv*(D+8)/64][8], box =
+// 16 rows x all 64-byte pieces x 8 elements, CU_TENSOR_MAP_SWIZZLE_64B (the
+// inner box is exactly the 64-byte swizzle span).  Same bytes as the bulk
+// copy of mode 0, with the 16-byte chunks of each 64-byte piece permuted as
+// swz64 undoes.  False unless the row is a whole number of 64-byte pieces
+// (at most 256 of them), the base is 16-byte aligned and the row count fits
+// the 32-bit coordinate.
+bool encode_pool_map_swz(CUtensorMap* m, const uint8_t* base, int64_t rows, int64_t kv, int64_t D) {
+  auto enc = tensor_map_encoder();
+  const int64_t row = kv * (D + 8);
+  if (!enc || reinterpret_cast<uintptr_t>(base) % 16 != 0 || row % 64 != 0 || row / 64 > 256) return false;
+  if (rows < 16 || rows > INT32_MAX) return false;
+  const cuuint64_t dims[3] = {8, (cuuint64_t)(row / 64), (cuuint64_t)rows};
+  const cuuint64_t strides[2] = {64, (cuuint64_t)row};
+  const cuuint32_t box[3] = {8, (cuuint32_t)(row / 64), (cuuint32_t)kTileTokens};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct Geometry {
   int G, nt, kvc, ngroups;
   bool pk;  // two tiles share one n-tile (G <= 4)
@@ -218,17 +241,23 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   const int qbuf = round_up(geo.kvc * geo.G * D * 2, 128);
   const int rbuf = layout == LAYOUT_PER_CHANNEL ? round_up(4 * geo.kvc * D * 2, 128) : 0;
   const int stage_offset = round_up(kHeaderBytes + nqbuf * (qbuf + rbuf), 128);
+  // swizzled stages start on a 1024-byte boundary: the kernel rounds the
+  // stage base up inside 1 KB of extra shared memory (stage sizes are whole
+  // KB there: 32 rows of 8*(D+8) bytes at D 64 / 128)
+  const bool swz = layout == LAYOUT_PAGED && p.paged_mode == 4;
+  if (swz && stage_bytes % 1024 != 0) return SLMT_ERR_UNSUPPORTED;
+  const int slack = swz ? 1024 : 0;
   const int want_ctas = ctas_per_sm(geo.kvc, geo.nt);
   const int threads = cta_threads(geo.kvc);
   const int budget = std::min(kSmemPerCtaMax, kSmemPerSm / want_ctas - kSmemReserved);
-  int stages = (budget - stage_offset) / stage_bytes;
+  int stages = (budget - stage_offset - slack) / stage_bytes;
   stages = std::min(stages, 6);
   if (stages < 2) {
-    stages = (kSmemPerCtaMax - stage_offset) / stage_bytes;
+    stages = (kSmemPerCtaMax - stage_offset - slack) / stage_bytes;
     stages = std::min(stages, 6);
     if (stages < 2) return SLMT_ERR_UNSUPPORTED;
   }
-  const int smem = stage_offset + stages * stage_bytes;
+  const int smem = stage_offset + stages * stage_bytes + slack;
   p.stages = stages;
   p.stage_bytes = stage_bytes;
   p.qbuf_bytes = qbuf;
@@ -236,12 +265,17 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.nqbuf = nqbuf;
   p.stage_offset = stage_offset;
 
-  DecodeFn fn = decode_fn(D, geo.nt, geo.pk, layout, geo.kvc, p.append != 0);
+  DecodeFn fn = decode_fn(D, geo.nt, geo.pk, layout, geo.kvc, p.append != 0, swz);
   const int occ = occupancy(dev, reinterpret_cast<const void*>(fn), threads, smem);
   if (occ <= 0) return SLMT_ERR_CUDA;
   const int64_t per_sm = std::min(occ, ctas_per_sm(geo.kvc, geo.nt));  // keeps the workspace bound
   int64_t nc = (int64_t)sms * per_sm;
-  const int64_t by_work = std::max<int64_t>(1, (chunks_upper + kMinChunksPerCta - 1) / kMinChunksPerCta);
+  // about kMinChunksPerCta chunks per CTA, but at least one CTA per segment
+  // while the grid has room: many short segments then start side by side
+  // instead of one after another in a few CTAs
+  const int64_t by_work = std::max<int64_t>(
+      std::max<int64_t>(1, (chunks_upper + kMinChunksPerCta - 1) / kMinChunksPerCta),
+      std::min<int64_t>((int64_t)geo.ngroups * p.num_seqs, chunks_upper));
   nc = std::max<int64_t>(1, std::min(nc, by_work));
   p.num_ctas = (int)nc;
 
@@ -490,7 +524,12 @@ int paged_decode_impl(
   p.bt_seq_stride = bt_seq_stride;
   p.max_blocks = (int)max_blocks_per_seq;
   if (geo.kvc == num_kv_heads && block_size % 16 == 0 && ca % 16 == 0)
-    p.paged_mode = 0;
+    // whole rows per page tile; swizzled (bank-conflict-free reads) where the
+    // SWZ kernels exist: 8 kv heads per CTA, head dim 64 or 128
+    p.paged_mode = (geo.kvc == 8 && (head_dim == 64 || head_dim == 128) &&
+                    encode_pool_map_swz(&p.tmap_k, kv_cache, num_blocks * block_size, num_kv_heads, head_dim))
+                       ? 4
+                       : 0;
   else if (block_size % 16 == 0 &&
            encode_pool_map(&p.tmap_k, kv_cache, num_blocks * block_size, num_kv_heads, head_dim, geo.kvc))
     p.paged_mode = 3;
@@ -626,8 +665,9 @@ extern "C" int slmt_per_channel_prefill(
   if (q_dtype != SLMT_DTYPE_F16 && q_dtype != SLMT_DTYPE_BF16) return SLMT_ERR_DTYPE;
   if (out_dtype != SLMT_DTYPE_F32 && out_dtype != SLMT_DTYPE_F16 && out_dtype != SLMT_DTYPE_BF16)
     return SLMT_ERR_DTYPE;
-  // codes are read as 4-byte words, q two elements at a time
-  if (reinterpret_cast<uintptr_t>(k_packed) % 4 != 0 || reinterpret_cast<uintptr_t>(v_packed) % 4 != 0 ||
+  // codes are copied in 8-byte pieces (rows of D/2 bytes are whole pieces),
+  // q read two elements at a time
+  if (reinterpret_cast<uintptr_t>(k_packed) % 8 != 0 || reinterpret_cast<uintptr_t>(v_packed) % 8 != 0 ||
       reinterpret_cast<uintptr_t>(q) % 2 != 0)
     return SLMT_ERR_ALIGN;
   return prefill_pc_launch(q, q_dtype == SLMT_DTYPE_BF16, q_head_stride, q_row_stride, k_packed, v_packed,

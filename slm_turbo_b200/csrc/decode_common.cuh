@@ -105,7 +105,9 @@ struct DecodeParams {
   int64_t bt_seq_stride;
   int max_blocks;
   int paged_mode;  // 0: one bulk copy per 16-token tile, 1: bulk copy per row, 2: cp.async rows,
-                   // 3: one 2-D tiled copy per 16-token tile of the group's heads (tmap_k)
+                   // 3: one 2-D tiled copy per 16-token tile of the group's heads (tmap_k),
+                   // 4: one 3-D tiled copy per 16-token tile of whole rows, 64-byte swizzled
+                   //    (tmap_k; the SWZ consumer reads through the swizzle)
   // contiguous layouts
   const uint8_t* k_codes;
   const uint8_t* v_codes;
@@ -159,9 +161,9 @@ using DecodeFn = void (*)(const DecodeParams);
 // Per head dim: the kernel for n-tiles nt, tile packing pk, kv heads per CTA
 // kvc, and (paged) whether the launch appends or (contiguous) the layout.
 // Defined in decode_d64.cu, decode_d80.cu, decode_d128.cu.
-DecodeFn decode_fn_64_paged(int nt, bool pk, int kvc, bool append);
-DecodeFn decode_fn_80_paged(int nt, bool pk, int kvc, bool append);
-DecodeFn decode_fn_128_paged(int nt, bool pk, int kvc, bool append);
+DecodeFn decode_fn_64_paged(int nt, bool pk, int kvc, bool append, bool swz);
+DecodeFn decode_fn_80_paged(int nt, bool pk, int kvc, bool append, bool swz);
+DecodeFn decode_fn_128_paged(int nt, bool pk, int kvc, bool append, bool swz);
 DecodeFn decode_fn_64_contig(int nt, bool pk, int layout, int kvc);
 DecodeFn decode_fn_80_contig(int nt, bool pk, int layout, int kvc);
 DecodeFn decode_fn_128_contig(int nt, bool pk, int layout, int kvc);

@@ -4,6 +4,8 @@
 
 namespace slmt {
 
-DecodeFn decode_fn_128_paged(int nt, bool pk, int kvc, bool append) { return paged_fn_d<128>(nt, pk, kvc, append); }
+DecodeFn decode_fn_128_paged(int nt, bool pk, int kvc, bool append, bool swz) {
+  return paged_fn_d<128>(nt, pk, kvc, append, swz);
+}
 
 }  // namespace slmt

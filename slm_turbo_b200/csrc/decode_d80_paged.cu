@@ -4,6 +4,8 @@
 
 namespace slmt {
 
-DecodeFn decode_fn_80_paged(int nt, bool pk, int kvc, bool append) { return paged_fn_d<80>(nt, pk, kvc, append); }
+DecodeFn decode_fn_80_paged(int nt, bool pk, int kvc, bool append, bool swz) {
+  return paged_fn_d<80>(nt, pk, kvc, append, swz);
+}
 
 }  // namespace slmt

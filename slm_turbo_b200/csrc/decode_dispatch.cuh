@@ -10,9 +10,16 @@ namespace slmt {
 // Instantiated per head dim, n-tiles, kv heads per CTA (compile-time row
 // strides, one consumer warp per kv head) and tile packing (PK: at most 4
 // query heads per kv head, so two tiles share one n-tile).  The paged
-// layout has a second instantiation that also appends the step's new tokens.
+// layout has a second instantiation that also appends the step's new tokens,
+// and, for whole rows of 8 kv heads at head dim 64 / 128, swizzled-stage
+// variants of both (paged mode 4).
 template <int D, int NT, bool PK, int KVC>
-DecodeFn paged_fn(bool append) {
+DecodeFn paged_fn(bool append, bool swz) {
+  if constexpr (KVC == 8 && (D == 64 || D == 128)) {
+    if (swz)
+      return append ? decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, true, true>
+                    : decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, false, true>;
+  }
   return append ? decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, true>
                 : decode_splitk_kernel<D, NT, LAYOUT_PAGED, KVC, PK, false>;
 }
@@ -24,12 +31,12 @@ DecodeFn contig_fn(int layout) {
 }
 
 template <int D, int NT, bool PK>
-DecodeFn paged_fn_kvc(int kvc, bool append) {
+DecodeFn paged_fn_kvc(int kvc, bool append, bool swz) {
   switch (kvc) {
-    case 8: return paged_fn<D, NT, PK, 8>(append);
-    case 4: return paged_fn<D, NT, PK, 4>(append);
-    case 2: return paged_fn<D, NT, PK, 2>(append);
-    default: return paged_fn<D, NT, PK, 1>(append);
+    case 8: return paged_fn<D, NT, PK, 8>(append, swz);
+    case 4: return paged_fn<D, NT, PK, 4>(append, false);
+    case 2: return paged_fn<D, NT, PK, 2>(append, false);
+    default: return paged_fn<D, NT, PK, 1>(append, false);
   }
 }
 
@@ -44,9 +51,9 @@ DecodeFn contig_fn_kvc(int layout, int kvc) {
 }
 
 template <int D>
-DecodeFn paged_fn_d(int nt, bool pk, int kvc, bool append) {
-  if (nt == 2) return paged_fn_kvc<D, 2, false>(kvc, append);
-  return pk ? paged_fn_kvc<D, 1, true>(kvc, append) : paged_fn_kvc<D, 1, false>(kvc, append);
+DecodeFn paged_fn_d(int nt, bool pk, int kvc, bool append, bool swz) {
+  if (nt == 2) return paged_fn_kvc<D, 2, false>(kvc, append, swz);
+  return pk ? paged_fn_kvc<D, 1, true>(kvc, append, swz) : paged_fn_kvc<D, 1, false>(kvc, append, swz);
 }
 
 template <int D>

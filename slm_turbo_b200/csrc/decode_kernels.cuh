@@ -190,6 +190,21 @@ struct StageView {
 };
 
 
+// Swizzled stages (paged mode 4): the tiled copy stores each 64-byte piece of
+// a stage with its 16-byte chunks permuted, chunk ^= bits 7-8 of the offset
+// (CU_TENSOR_MAP_SWIZZLE_64B, stage bases 1024-byte aligned).  Byte offset o
+// of the unswizzled stage lies at swz64(o); 8-byte reads never straddle a
+// chunk.  Row offsets of 8 and 16 tokens are multiples of 512 bytes (a row is
+// a multiple of 64), so they commute with the swizzle.
+__device__ __forceinline__ uint32_t swz64(uint32_t o) { return o ^ (((o >> 7) & 3u) << 4); }
+
+// With swizzled stages, MMA fragment row k of a 16-token tile holds token
+// tok_perm(k) (bits 0 and 1 swapped): the 8 rows one shared load touches
+// then spread over all 32 banks.  A permutation of the tokens of a tile
+// changes nothing in the result as long as scores, masks, rulers and V rows
+// all use it.
+__device__ __forceinline__ int tok_perm(int k) { return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1); }
+
 // ------------------------------------------------------------------ producer --
 // Page ids of 32 consecutive 16-token tiles of sequence s, one per lane.
 __device__ __forceinline__ int64_t page_window(const DecodeParams& p, int s, int tile0, int ntile) {
@@ -353,7 +368,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
     // prefetched state: page-id windows of this segment (current, next) and
     // the next segment's length and first window
     // whole 16-token tiles per copy (mode 0: contiguous bulk; mode 3: 2-D tiled)
-    const bool pg_mode0 = (LAYOUT == LAYOUT_PAGED) && (p.paged_mode == 0 || p.paged_mode == 3);
+    const bool pg_mode0 = (LAYOUT == LAYOUT_PAGED) && (p.paged_mode == 0 || p.paged_mode >= 3);
     int pg_base = 2 * chunk;
     int64_t pg_cur = 0, pg_nxt = 0, pg_seg = 0;
     int ns = 0, nkg = 0, nL = 0;
@@ -443,7 +458,13 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
           __syncwarp();
           if (lane == 0) {
             mbar_arrive_expect_tx(fb, tx);
-            if (p.paged_mode == 3) {
+            if (p.paged_mode == 4) {
+              // whole rows of 16 tokens: 64-byte pieces x rows, swizzled
+              if (ok0) tma_load_3d_hint(dst, &p.tmap_k, 0, 0, (int)(ph0 * bs + tok0 % bs), fb, policy);
+              if (ok1)
+                tma_load_3d_hint(dst + tile_bytes, &p.tmap_k, 0, 0, (int)(ph1 * bs + (tok0 + kTileTokens) % bs), fb,
+                                 policy);
+            } else if (p.paged_mode == 3) {
               // the group's heads of 16 token rows: x = first 8-byte element of
               // head kg*kvc in a row (a multiple of 16 bytes), y = token row
               const int x = kg * p.kvc * (SLOT / 8);
@@ -707,7 +728,9 @@ __device__ void merge_segment(const DecodeParams& p, const MergeJob& job, int i0
   const int tid = threadIdx.x;
   const int hg = p.kvc * p.G;
   const int np = job.ncov;
-  int nb = min(np, 16);
+  // partials per pass: up to 64 (a segment split over many CTAs, e.g. one
+  // long sequence over the whole grid, then merges in few dependent passes)
+  int nb = min(np, 64);
   while (nb > 1 && nb * (D + 2) > scr_floats) nb >>= 1;
   const int hp = max(1, min(min(hg, scr_floats / (nb * (D + 2))), IPT * NTHR / Q));
   const int64_t row0 = (int64_t)(job.c_first + job.e_seg) * hg;  // partial i, head h: row0 + i*hg + h
@@ -820,7 +843,7 @@ struct WarpState {
 // softmax runs on useful columns only; PV feeds each tile its own columns.
 // The two column halves are two online-softmax streams over the even and
 // odd tiles, combined at the segment end.
-template <int D, int NT, int LAYOUT, int KVC, bool MASK, bool PK>
+template <int D, int NT, int LAYOUT, int KVC, bool MASK, bool PK, bool SWZ>
 __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D, NT>& w,
                                               const StageView<D, LAYOUT, KVC>& sv, int nvalid,
                                               uint64_t* empty_bar, bool release) {
@@ -836,10 +859,31 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   // QK / scores use token rows g and g+8 of each tile, PV rows 2r, 2r+1,
   // 2r+8, 2r+9
   using SV = StageView<D, LAYOUT, KVC>;
-  const uint8_t* krow = sv.k(g);  // + a*d16 + h*d8 -> row 16a + g + 8h
-  const uint8_t* rrow = sv.rulers(g);
-  const uint8_t* vrow0 = sv.v(2 * r);
-  const uint8_t* vrow1 = sv.v(2 * r + 1);
+  static_assert(!SWZ || (LAYOUT == LAYOUT_PAGED && (D == 64 || D == 128) && SV::kRow % 64 == 0),
+                "swizzled stages: whole 64-byte rows, 8-byte aligned reads");
+  // fragment row -> token row of the tile (identity unless swizzled)
+  const int tg = SWZ ? tok_perm(g) : g;
+  const int tv0 = SWZ ? tok_perm(2 * r) : 2 * r;
+  const int tv1 = SWZ ? tok_perm(2 * r + 1) : 2 * r + 1;
+  const uint8_t* krow = sv.k(tg);  // + a*d16 + h*d8 -> row 16a + tg + 8h
+  const uint8_t* rrow = sv.rulers(tg);
+  const uint8_t* vrow0 = sv.v(tv0);
+  const uint8_t* vrow1 = sv.v(tv1);
+  // swizzled: sv.base is the stage base (1024-aligned); the warp's head and
+  // every byte offset within a row go through swz64, and the reads use
+  // 32-bit shared addresses
+  uint32_t kq0 = 0, kq1 = 0, rq = 0, vq0 = 0, vq1 = 0;
+  if constexpr (SWZ) {
+    const uint32_t sb = smem_addr(sv.base);
+    const uint32_t hb = (uint32_t)(threadIdx.x >> 5) * (D + 8);
+    const uint32_t ok = (uint32_t)(tg * SV::kRow) + hb;
+    kq0 = sb + swz64(ok + 8u * r);
+    kq1 = sb + swz64(ok + 32u + 8u * r);
+    rq = sb + swz64(ok + D);
+    const uint32_t ov = (uint32_t)(tv0 * SV::kRow) + hb + D / 2 + (uint32_t)(g * (D / 16));
+    vq0 = sb + swz64(ov);
+    vq1 = sb + swz64(ov + 2 * SV::kRow);  // tok_perm(2r+1) = tok_perm(2r) + 2
+  }
   static_assert(!PK || NT == 1, "tile packing needs one n-tile");
   constexpr int NA = PK ? 1 : 2;     // score tiles held per thread
   const int at = PK ? (r >> 1) : 0;  // PK: the tile of this thread's columns
@@ -858,7 +902,23 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
     }
     uint32_t ka[QW], kb[QW];
     const uint8_t* k0 = krow + a * SV::d16;
-    if constexpr (QB == 16) {
+    if constexpr (SWZ) {
+      // thread-constant swizzled addresses of bytes [8r, +8) and [32+8r, +8)
+      // (D=128) or [8r, +8) (D=64) of rows tg and tg+8
+      uint2 x = lds64(kq0 + a * SV::d16), y = lds64(kq0 + a * SV::d16 + SV::d8);
+      ka[0] = x.x;
+      ka[1] = x.y;
+      kb[0] = y.x;
+      kb[1] = y.y;
+      if constexpr (QB == 16) {
+        x = lds64(kq1 + a * SV::d16);
+        y = lds64(kq1 + a * SV::d16 + SV::d8);
+        ka[2] = x.x;
+        ka[3] = x.y;
+        kb[2] = y.x;
+        kb[3] = y.y;
+      }
+    } else if constexpr (QB == 16) {
       load_bytes<8, 8>(k0 + 8 * r, ka);
       load_bytes<8, 8>(k0 + 32 + 8 * r, ka + 2);
       load_bytes<8, 8>(k0 + SV::d8 + 8 * r, kb);
@@ -910,7 +970,12 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
 #pragma unroll
     for (int a = 0; a < NA; ++a)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) rr[a][h] = *reinterpret_cast<const uint2*>(rrow + tile(a) * SV::r16 + h * SV::r8);
+      for (int h = 0; h < 2; ++h) {
+        if constexpr (SWZ)
+          rr[a][h] = lds64(rq + tile(a) * SV::r16 + h * SV::r8);
+        else
+          rr[a][h] = *reinterpret_cast<const uint2*>(rrow + tile(a) * SV::r16 + h * SV::r8);
+      }
   }
   auto ruler_k = [&](int a, int h) -> float2 {
     if (LAYOUT == LAYOUT_PER_CHANNEL) return make_float2(p.use_quant ? -1.f : 0.f, 1.f);
@@ -924,7 +989,7 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
 #pragma unroll
   for (int a = 0; a < NA; ++a)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * tile(a) + g + 8 * h) < nvalid;
+    for (int h = 0; h < 2; ++h) val[a][h] = !MASK || (16 * tile(a) + tg + 8 * h) < nvalid;
 
   // ---- scores + online softmax (log2 domain, lazy rescale) ----
   const float sl2 = p.scale_log2;
@@ -1036,10 +1101,26 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
       }
     }
     uint32_t vw[4][VW];
-    load_bytes<VB, VALIGN>(vrow0 + a * SV::d16 + g * VB, vw[0]);
-    load_bytes<VB, VALIGN>(vrow1 + a * SV::d16 + g * VB, vw[1]);
-    load_bytes<VB, VALIGN>(vrow0 + a * SV::d16 + SV::d8 + g * VB, vw[2]);
-    load_bytes<VB, VALIGN>(vrow1 + a * SV::d16 + SV::d8 + g * VB, vw[3]);
+    if constexpr (SWZ) {
+      // VB = 8 (D=128) or 4 (D=64) bytes of rows tv0, tv1 (+8)
+      const uint32_t ad[4] = {vq0 + a * SV::d16, vq1 + a * SV::d16, vq0 + a * SV::d16 + SV::d8,
+                              vq1 + a * SV::d16 + SV::d8};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (VB == 8) {
+          const uint2 x = lds64(ad[i]);
+          vw[i][0] = x.x;
+          vw[i][1] = x.y;
+        } else {
+          vw[i][0] = lds32(ad[i]);
+        }
+      }
+    } else {
+      load_bytes<VB, VALIGN>(vrow0 + a * SV::d16 + g * VB, vw[0]);
+      load_bytes<VB, VALIGN>(vrow1 + a * SV::d16 + g * VB, vw[1]);
+      load_bytes<VB, VALIGN>(vrow0 + a * SV::d16 + SV::d8 + g * VB, vw[2]);
+      load_bytes<VB, VALIGN>(vrow1 + a * SV::d16 + SV::d8 + g * VB, vw[3]);
+    }
     if (a == 1 && release) {  // every shared-memory read of the stage is done: release it
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar);
@@ -1111,7 +1192,7 @@ __device__ __forceinline__ void append_token(const DecodeParams& p, SmemHeader* 
   __syncwarp();
 }
 
-template <int D, int NT, int LAYOUT, int KVC, bool PK, bool APPEND>
+template <int D, int NT, int LAYOUT, int KVC, bool PK, bool APPEND, bool SWZ>
 __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
                                 const uint8_t* qbuf, const uint8_t* rbuf,
                                 const uint8_t* stg) {
@@ -1259,16 +1340,19 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
           // the segment's newest token is the last valid row of this chunk:
           // its slot, quantized at the segment start, replaces the staged copy
           // (read from the cache before this launch wrote it)
-          uint8_t* row = const_cast<uint8_t*>(st) + (nvalid - 1) * StageView<D, LAYOUT, KVC>::kRow + j * (D + 8);
-          if (lane < (D + 8) / 8)
-            reinterpret_cast<uint2*>(row)[lane] = reinterpret_cast<const uint2*>(hdr->newslot[j])[lane];
+          const uint32_t ro = (uint32_t)((nvalid - 1) * StageView<D, LAYOUT, KVC>::kRow + j * (D + 8));
+          if (lane < (D + 8) / 8) {
+            const uint32_t o = ro + 8u * lane;
+            *reinterpret_cast<uint2*>(const_cast<uint8_t*>(st) + (SWZ ? swz64(o) : o)) =
+                reinterpret_cast<const uint2*>(hdr->newslot[j])[lane];
+          }
           fence_proxy_async_shared();  // before the producer's next copy reuses the stage
           __syncwarp();
         }
       }
       StageView<D, LAYOUT, KVC> sv;
       if (LAYOUT == LAYOUT_PAGED) {
-        sv.base = st + j * (D + 8);
+        sv.base = SWZ ? st : st + j * (D + 8);  // swizzled: offsets are taken from the stage base
         sv.rul = nullptr;
       } else {
         sv.base = st + j * kChunkTokens * (D / 2);
@@ -1278,9 +1362,9 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
       // segment's output or partial is written
       const bool rel = !(flags & kFlagLast);
       if (nvalid == kChunkTokens)
-        consume_chunk<D, NT, LAYOUT, KVC, false, PK>(p, w, sv, nvalid, &hdr->empty[stage], rel);
+        consume_chunk<D, NT, LAYOUT, KVC, false, PK, SWZ>(p, w, sv, nvalid, &hdr->empty[stage], rel);
       else
-        consume_chunk<D, NT, LAYOUT, KVC, true, PK>(p, w, sv, nvalid, &hdr->empty[stage], rel);
+        consume_chunk<D, NT, LAYOUT, KVC, true, PK, SWZ>(p, w, sv, nvalid, &hdr->empty[stage], rel);
     }
 
     if (flags & kFlagLast) {
@@ -1429,7 +1513,10 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 // APPEND (paged layout only): the launch also quantizes each sequence's new
 // token into the cache (slmt_paged_append_decode); a separate instantiation,
 // so the plain decode carries none of that code.
-template <int D, int NT, int LAYOUT, int KVC, bool PK, bool APPEND = false>
+// SWZ (paged, whole rows, D 64/128): stages filled by the 64-byte swizzled
+// tiled copy (paged mode 4) and read through the swizzle; the host reserves
+// 1 KB more shared memory so the stage base can be rounded up to 1024 bytes.
+template <int D, int NT, int LAYOUT, int KVC, bool PK, bool APPEND = false, bool SWZ = false>
 __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
     decode_splitk_kernel(const __grid_constant__ DecodeParams p) {
   static_assert(!APPEND || LAYOUT == LAYOUT_PAGED, "the fused append writes the paged layout");
@@ -1438,6 +1525,7 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
   uint8_t* qbuf = smem + kHeaderBytes;
   uint8_t* rbuf = qbuf + p.nqbuf * p.qbuf_bytes;
   uint8_t* stg = smem + p.stage_offset;
+  if constexpr (SWZ) stg += (1024u - (smem_addr(stg) & 1023u)) & 1023u;
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(&hdr->full[i], 33);  // producer lane 0 + 32 cp.async arrivals
@@ -1458,7 +1546,7 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
   if (threadIdx.x >= KVC * 32)
     decode_producer<D, LAYOUT, APPEND>(p, hdr, qbuf, rbuf, stg);
   else
-    decode_consumer<D, NT, LAYOUT, KVC, PK, APPEND>(p, hdr, qbuf, rbuf, stg);
+    decode_consumer<D, NT, LAYOUT, KVC, PK, APPEND, SWZ>(p, hdr, qbuf, rbuf, stg);
 }
 
 }  // namespace slmt

@@ -14,13 +14,15 @@
 //                   continuation chunk of a prompt over its cached prefix
 //                   (chunked prefill, prefix caching).
 //
-// One CTA = 4 warps = 64 query rows of one query head (warp w owns rows
-// m0+16w .. m0+16w+15).  The CTA walks the keys in chunks of 64 tokens:
-//   1. all 128 threads read the chunk's packed K and V codes of the kv head
-//      as 4-byte words and dequantize them ONCE for all 64 rows into shared
+// One CTA = 4 warps per query head x 64 query rows, for one or two query
+// heads of a kv group (warp w owns rows m0+16(w%4) .. +15 of head w/4).  The CTA walks the keys in chunks of 64 tokens:
+//   1. the chunk's packed K and V codes (and, paged, token rulers) arrive in
+//      a raw shared-memory buffer by 8-byte cp.async, issued while the
+//      previous chunk is dequantized and computed (the paged layout resolves
+//      the slot rows through the block table one chunk further ahead); all
+//      128 threads then dequantize them ONCE for all 64 rows into shared
 //      memory as fp16 (rows padded to D+8 halves so ldmatrix rows fall in
-//      distinct banks); the paged layout first resolves the chunk's 64 slot
-//      offsets and token rulers through the block table into shared memory;
+//      distinct banks);
 //   2. each warp: S[16 x 64] = Q K^T on the tensor core (m16n8k16, fp32
 //      accumulation; Q A-fragments held in registers for the whole CTA, K
 //      B-fragments by ldmatrix), causal / length mask, online softmax in the
@@ -30,6 +32,8 @@
 // K/V are read once per 64 query rows instead of once per row.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <atomic>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -112,23 +116,47 @@ __device__ __forceinline__ int64_t pf_slot_row(const PrefillParams& p, int req, 
   return ((ph * p.block_size + t % p.block_size) * p.KV + kvh) * (int64_t)(D + 8);
 }
 
+// Shared memory of one CTA (dynamic): the dequantized chunk (K and V rows
+// padded to D+8 halves) and two raw-code buffers, chunk c+1 arriving by
+// cp.async while chunk c is dequantized and computed.  A raw buffer holds
+// the chunk's K codes [64][D/2], V codes [64][D/2] and, paged, the token
+// rulers [64][8] (k_min, k_step, v_min, v_step).
 template <int D, int LAYOUT>
-__global__ void __launch_bounds__(128) prefill_kernel(const __grid_constant__ PrefillParams p) {
+constexpr int pf_raw_bytes() {
+  return 2 * kPfTokens * (D / 2) + (LAYOUT == PF_PAGED ? kPfTokens * 8 : 0);
+}
+template <int D, int LAYOUT>
+constexpr int pf_smem_bytes() {
+  return 2 * kPfTokens * (D + 8) * 2 + 2 * pf_raw_bytes<D, LAYOUT>();
+}
+
+__device__ __forceinline__ void pf_cp_async8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// HPC query heads of one kv group per CTA (4 warps each, rows m0.. m0+63):
+// the dequantized chunk is shared by all of them.
+template <int D, int LAYOUT, int HPC>
+__global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constant__ PrefillParams p) {
+  constexpr int NTHR = 128 * HPC;
   constexpr int KS = D / 16;   // k-steps of QK
   constexpr int NTO = D / 8;   // n-tiles of O
   constexpr int LD = D + 8;    // smem row stride in halves (odd multiple of 16 bytes)
   constexpr int NTS = kPfTokens / 8;  // n-tiles of S per chunk
   constexpr int WPR = D / 8;          // 4-byte code words per token row
   constexpr int WORDS = kPfTokens * WPR;
-  __shared__ __align__(16) __half ksh[kPfTokens * LD];
-  __shared__ __align__(16) __half vsh[kPfTokens * LD];
-  __shared__ __align__(16) __half rul[4][D];          // per-channel: k scale, k zero, v scale, v zero
-  __shared__ int64_t slot_off[2][kPfTokens];          // paged: slot row of each chunk token (-1: none)
-  __shared__ __align__(8) uint2 tok_rul[2][kPfTokens];  // paged: (k_min,k_step), (v_min,v_step)
+  constexpr int PPR = D / 16;         // 8-byte pieces per token row of K (or V)
+  constexpr int RAW = pf_raw_bytes<D, LAYOUT>();
+  extern __shared__ __align__(16) uint8_t pf_smem[];
+  __half* ksh = reinterpret_cast<__half*>(pf_smem);
+  __half* vsh = ksh + kPfTokens * LD;
+  uint8_t* raw = reinterpret_cast<uint8_t*>(vsh + kPfTokens * LD);  // [2][RAW]
+  __shared__ __align__(16) __half rul[4][D];  // per-channel: k scale, k zero, v scale, v zero
+  __shared__ int64_t slot_off[2][kPfTokens];  // paged: slot row of each chunk token (-1: none)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, r = lane & 3;
-  const int h = blockIdx.y, kvh = h / p.G;
+  const int h = blockIdx.y * HPC + (warp >> 2), kvh = h / p.G;  // HPC divides G: one kv head per CTA
   const int m0 = blockIdx.x * kPfRows;
 
   // ---- this CTA's problem: rows [row0, row0+M), keys [0, S), row i
@@ -139,18 +167,19 @@ __global__ void __launch_bounds__(128) prefill_kernel(const __grid_constant__ Pr
     row0 = p.query_start_loc[req];
     M = max(p.query_start_loc[req + 1] - row0, 0);
     const int sraw = p.seq_lens[req];
-    S = (int)min((int64_t)max(sraw, 0), p.len_cap);
-    if (tid == 0 && blockIdx.x == 0 && h == 0) {
+    if (sraw <= 0) return;  // a request without keys is skipped: its rows are left as they are
+    S = (int)min((int64_t)sraw, p.len_cap);
+    if (tid == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
       if ((int64_t)sraw > p.len_cap) pf_set_err(p, SLMT_DEVERR_SEQ_LEN);
       if (M > (int)gridDim.x * kPfRows) pf_set_err(p, SLMT_DEVERR_SEQ_LEN);  // rows past max_query_len
     }
     off = S - M;
   }
   if (m0 >= M) return;  // whole CTA: no row of this tile exists
-  const int mw = m0 + warp * 16;  // this warp's first row (relative)
+  const int mw = m0 + (warp & 3) * 16;  // this warp's first row (relative)
 
   if (LAYOUT == PF_PER_CHANNEL && p.use_quant && S > 0) {  // rulers unused (and may be NULL) otherwise
-    for (int i = tid; i < 4 * D; i += 128) {
+    for (int i = tid; i < 4 * D; i += NTHR) {
       const uint16_t* src = (i < D) ? p.k_scale : (i < 2 * D) ? p.k_zero : (i < 3 * D) ? p.v_scale : p.v_zero;
       reinterpret_cast<uint16_t*>(&rul[0][0])[i] = src[(int64_t)kvh * D + (i % D)];
     }
@@ -191,39 +220,71 @@ __global__ void __launch_bounds__(128) prefill_kernel(const __grid_constant__ Pr
   const int kend = p.causal ? max(0, min(S, off + row_last + 1)) : S;
   const int64_t kvbase = (int64_t)kvh * S * (D / 2);  // per-channel codes of this kv head
 
-  // paged: resolve a chunk's slot rows and token rulers (threads 0..63)
+  // paged: resolve a chunk's slot rows through the block table (threads 0..63)
   auto prep = [&](int t0, int buf) {
     if (LAYOUT == PF_PAGED && tid < kPfTokens) {
       const int t = t0 + tid;
-      int64_t so = -1;
-      uint2 ru = make_uint2(0u, 0u);
-      if (t < S) {
-        so = pf_slot_row(p, req, t, kvh, D);
-        if (so >= 0) ru = *reinterpret_cast<const uint2*>(p.cache + so + D);
+      slot_off[buf][tid] = (t < S) ? pf_slot_row(p, req, t, kvh, D) : -1;
+    }
+  };
+  // start the copies of chunk t0 into raw buffer `rb` (8-byte pieces; a
+  // token that does not exist or whose page is bad is written as zeros)
+  auto issue = [&](int t0, int rb) {
+    uint8_t* dst = raw + rb * RAW;
+    const uint32_t d0 = smem_addr(dst);
+    constexpr int NPC = 2 * kPfTokens * PPR + (LAYOUT == PF_PAGED ? kPfTokens : 0);
+    for (int i = tid; i < NPC; i += NTHR) {
+      int tok, boff;
+      const uint8_t* src = nullptr;
+      if (i < 2 * kPfTokens * PPR) {
+        const int isv = i >= kPfTokens * PPR;
+        const int pc = isv ? i - kPfTokens * PPR : i;
+        tok = pc / PPR;
+        const int pp = pc % PPR;
+        boff = isv * kPfTokens * (D / 2) + tok * (D / 2) + 8 * pp;
+        if (LAYOUT == PF_PER_CHANNEL) {
+          if (t0 + tok < S) src = (isv ? p.v_codes : p.k_codes) + kvbase + (int64_t)(t0 + tok) * (D / 2) + 8 * pp;
+        } else {
+          const int64_t so = slot_off[rb][tok];
+          if (so >= 0) src = p.cache + so + (isv ? D / 2 : 0) + 8 * pp;
+        }
+      } else {  // paged token rulers
+        tok = i - 2 * kPfTokens * PPR;
+        boff = 2 * kPfTokens * (D / 2) + tok * 8;
+        const int64_t so = slot_off[rb][tok];
+        if (so >= 0) src = p.cache + so + D;
       }
-      slot_off[buf][tid] = so;
-      tok_rul[buf][tid] = ru;
+      if (src)
+        pf_cp_async8(d0 + boff, src);
+      else
+        *reinterpret_cast<uint2*>(dst + boff) = make_uint2(0u, 0u);
     }
   };
   prep(0, 0);
+  prep(kPfTokens, 1);
   __syncthreads();
+  if (kend > 0) issue(0, 0);
 
   int buf = 0;
   for (int t0 = 0; t0 < kend; t0 += kPfTokens, buf ^= 1) {
-    // ---- 1. dequantize the chunk's K and V into shared memory ----
+    // ---- 1. chunk t0 has landed; start chunk t0+64, resolve chunk t0+128 ----
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    if (t0 + kPfTokens < kend) issue(t0 + kPfTokens, buf ^ 1);  // its slot rows: slot_off[buf ^ 1]
+    if (t0 + 2 * kPfTokens < kend) prep(t0 + 2 * kPfTokens, buf);  // slot_off[buf] was chunk t0's
+    // ---- 2. dequantize the chunk's K and V into shared memory ----
     // a word holds the 8 codes of dims 8wr .. 8wr+7 (byte e/2, low nibble for
     // even dims); a token row is a whole number of words for every D
-    for (int i = tid; i < 2 * WORDS; i += 128) {
+    const uint8_t* src = raw + buf * RAW;
+    for (int i = tid; i < 2 * WORDS; i += NTHR) {
       const int isv = i >= WORDS;
       const int w = isv ? i - WORDS : i;
       const int tok = w / WPR, wr = w % WPR;
       const int d0 = 8 * wr;
-      uint32_t word = 0u;
+      const uint32_t word =
+          *reinterpret_cast<const uint32_t*>(src + isv * kPfTokens * (D / 2) + tok * (D / 2) + 4 * wr);
       float vals[8];
       if (LAYOUT == PF_PER_CHANNEL) {
-        if (t0 + tok < S)
-          word = reinterpret_cast<const uint32_t*>((isv ? p.v_codes : p.k_codes) + kvbase +
-                                                   (int64_t)(t0 + tok) * (D / 2))[wr];
         const __half* sc = rul[isv ? 2 : 0];
         const __half* zp = rul[isv ? 3 : 1];
 #pragma unroll
@@ -232,9 +293,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(const __grid_constant__ Pr
           vals[e] = p.use_quant ? (c - __half2float(zp[d0 + e])) * __half2float(sc[d0 + e]) : c;
         }
       } else {
-        const int64_t so = slot_off[buf][tok];
-        if (so >= 0) word = *reinterpret_cast<const uint32_t*>(p.cache + so + (isv ? D / 2 : 0) + 4 * wr);
-        const uint32_t rp = isv ? tok_rul[buf][tok].y : tok_rul[buf][tok].x;  // (min, step)
+        const uint2 ru = *reinterpret_cast<const uint2*>(src + 2 * kPfTokens * (D / 2) + tok * 8);
+        const uint32_t rp = isv ? ru.y : ru.x;  // (min, step)
         const float2 mn_st = __half22float2(*reinterpret_cast<const __half2*>(&rp));
 #pragma unroll
         for (int e = 0; e < 8; ++e) vals[e] = fmaf((float)((word >> (4 * e)) & 15u), mn_st.y, mn_st.x);
@@ -327,8 +387,6 @@ __global__ void __launch_bounds__(128) prefill_kernel(const __grid_constant__ Pr
         }
       }
     }
-    if (t0 + kPfTokens < kend) prep(t0 + kPfTokens, buf ^ 1);  // the other buffer: last read a chunk ago
-    __syncthreads();
   }
 
   // ---- normalise and store rows mw+g, mw+g+8 ----
@@ -349,15 +407,35 @@ __global__ void __launch_bounds__(128) prefill_kernel(const __grid_constant__ Pr
   }
 }
 
+// One instantiation: opt it into its dynamic shared memory (more than the
+// default 48 KB at D=128) the first time, then launch.
+template <int D, int LAYOUT, int HPC>
+int prefill_launch_d(const PrefillParams& p, dim3 grid, cudaStream_t st) {
+  constexpr int smem = pf_smem_bytes<D, LAYOUT>();
+  static std::atomic<int> opted{-1};  // device the attribute was last set for
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SLMT_ERR_CUDA;
+  if (opted.load(std::memory_order_acquire) != dev) {
+    if (cudaFuncSetAttribute(prefill_kernel<D, LAYOUT, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return SLMT_ERR_CUDA;
+    }
+    opted.store(dev, std::memory_order_release);
+  }
+  grid.y /= HPC;
+  prefill_kernel<D, LAYOUT, HPC><<<grid, 128 * HPC, smem, st>>>(p);
+  return launch_status();
+}
+
+// Two query heads per CTA when the group has an even number of them (their
+// shared chunk is dequantized once), else one.
 template <int LAYOUT>
 int prefill_launch(const PrefillParams& p, int head_dim, dim3 grid, cudaStream_t st) {
-  if (head_dim == 64)
-    prefill_kernel<64, LAYOUT><<<grid, 128, 0, st>>>(p);
-  else if (head_dim == 80)
-    prefill_kernel<80, LAYOUT><<<grid, 128, 0, st>>>(p);
-  else
-    prefill_kernel<128, LAYOUT><<<grid, 128, 0, st>>>(p);
-  return launch_status();
+  const bool two = p.G % 2 == 0;
+  if (head_dim == 64) return two ? prefill_launch_d<64, LAYOUT, 2>(p, grid, st) : prefill_launch_d<64, LAYOUT, 1>(p, grid, st);
+  if (head_dim == 80) return two ? prefill_launch_d<80, LAYOUT, 2>(p, grid, st) : prefill_launch_d<80, LAYOUT, 1>(p, grid, st);
+  return two ? prefill_launch_d<128, LAYOUT, 2>(p, grid, st) : prefill_launch_d<128, LAYOUT, 1>(p, grid, st);
 }
 
 int prefill_pc_launch(const void* q, int q_bf16, int64_t q_head_stride, int64_t q_row_stride,

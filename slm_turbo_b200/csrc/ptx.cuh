@@ -102,6 +102,29 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0,
       : "memory");
 }
 
+// 8- and 4-byte shared-memory loads at a 32-bit shared address.  Volatile:
+// they stay after the mbarrier wait that publishes the bytes.
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// As tma_load_3d with an L2 cache policy (createpolicy) for the loaded lines.
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const void* tmap, int c0, int c1, int c2,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
 // Order this thread's earlier generic-proxy accesses to shared memory before
 // later async-proxy (TMA) accesses of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_shared() {

@@ -381,9 +381,10 @@ def kv_prefill_paged(q, kv_cache, block_tables, query_start_loc, seq_lens, max_q
     seq_lens[r] tokens, which must already be stored in kv_cache [NB, bs, KV,
     D+8]; row i attends causally to keys [0, seq_lens[r] - n_r + i + 1)
     through block_tables [R, max_blocks] (int32/int64).  query_start_loc
-    [R+1] and seq_lens [R] int32 on the device; max_query_len (host int)
-    bounds n_r.  Returns out [N, Hq, D] (fp32 by default, or the given
-    ``out``).  Replaces the reference adapter's raw-K/V SDPA prefill for
+    [R+1] and seq_lens [R] int32 on the device; a request with seq_lens 0
+    is skipped (its rows of ``out`` are not written); max_query_len (host
+    int) bounds n_r of the others.  Returns out [N, Hq, D] (fp32 by default,
+    or the given ``out``).  Replaces the reference adapter's raw-K/V SDPA prefill for
     chunks with a cached prefix (adapters/vllm_adapter.py:218-243).
     """
     L = _lib.load()

@@ -137,3 +137,23 @@ def test_paged_prefill_flags_bad_page_and_overlong():
     assert (out[64:] == -7.0).all()
     assert_close(out[:64].cpu().numpy(), _expected(st2, 2, 16, False)[:64], what="first tile")
     assert kd.read_device_errors(dev) == 0
+
+
+def test_paged_prefill_skips_requests_without_keys():
+    """seq_lens 0 marks a request the caller attends some other way (the
+    vLLM impl's fresh prompts): its rows are left untouched and its row
+    count is not checked against max_query_len."""
+    kd = _kd()
+    st = _build([(50, 20), (0, 300), (10, 5)], 8, 2, 64, 16, seed=8)
+    dev = torch.device("cuda")
+    sl = st["sl"].clone()
+    sl[1] = 0
+    out = torch.full((325, 8, 64), -3.0, device=dev)
+    kd.kv_prefill_paged(st["q"].to(dev), st["cache"].to(dev), st["bt"].to(dev), st["qsl"].to(dev),
+                        sl.to(dev), 20, block_size=16, num_kv_heads=2, out=out)
+    torch.cuda.synchronize()
+    assert kd.read_device_errors(dev) == 0
+    assert (out[20:320] == -3.0).all()
+    want = _expected(st, 2, 16, False)
+    assert_close(out[:20].cpu().numpy(), want[:20], what="request 0")
+    assert_close(out[320:].cpu().numpy(), want[320:], what="request 2")
