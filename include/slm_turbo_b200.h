@@ -61,6 +61,8 @@ extern "C" {
 #define SLMT_DEVERR_SLOT 2u     /* slot_mapping entry beyond the cache          */
 #define SLMT_DEVERR_TIMEOUT 4u  /* a pipeline wait exceeded its time limit      */
 #define SLMT_DEVERR_SEQ_LEN 8u  /* sequence length above the table capacity     */
+#define SLMT_DEVERR_PLACEMENT 16u /* a decode grid that should hold two CTAs per SM
+                                     did not (its SM-aware chunk ranges are incomplete) */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int slmt_version(void);

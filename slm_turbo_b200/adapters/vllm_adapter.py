@@ -138,7 +138,7 @@ class _ErrorWatch:
                 logger.error("slm-turbo kernels set device error bits 0x%x", bits)
                 raise RuntimeError(f"slm-turbo kernels reported device error bits 0x{bits:x} "
                                    "(1 bad block id, 2 slot beyond the cache, 4 wait timeout, "
-                                   "8 length above the block table)")
+                                   "8 length above the block table, 16 unexpected CTA placement)")
         self.host.copy_(_lib.error_word(self.device), non_blocking=True)
         if self.event is None:
             self.event = torch.cuda.Event()

@@ -11,6 +11,14 @@ namespace slmt {
 
 namespace {
 
+// Chunk shares of the first and the second CTA on an SM (SM-aware pieces):
+// 6:5 measured best on C3 (5:4, 4:3 and 1:1 beside it).
+constexpr int kPartWeightFirst = 6;
+constexpr int kPartWeightSecond = 5;
+// Cost of a segment start in eighths of a chunk (q staging, fragments,
+// output or partial and its publication), for the weighted partition: 24
+// measured best on C3 (0, 8, 16, 32 beside it: 77.3, 76.5, 75.7, 74.9 vs 74.5 us).
+constexpr int kSegStartCost = 24;
 constexpr int kMinChunksPerCta = 4;    // do not split below ~128 tokens per CTA
 constexpr int kSmemPerSm = 233472;     // 228 KB shared memory per SM (sm_100)
 constexpr int kSmemPerCtaMax = 232448; // 227 KB opt-in per CTA
@@ -288,6 +296,18 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return SLMT_ERR_ALIGN;
   uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
   p.seg_count = reinterpret_cast<int32_t*>(w);
+  // SM-aware pieces need exactly two CTAs on every SM: a full grid of a
+  // kernel whose registers allow no more than two per SM (8 kv heads, one
+  // n-tile), and room for the arrival words after the segment words
+  p.sm_weighted = (geo.kvc == 8 && geo.nt == 1 && nc == 2LL * sms && ctas_per_sm(geo.kvc, geo.nt) == 2 &&
+                   creg >= (segments + sms + 1) * 4)
+                      ? 1
+                      : 0;
+  p.num_sms = sms;
+  p.part_w0 = kPartWeightFirst;
+  p.part_w1 = kPartWeightSecond;
+  p.seg_cost = kSegStartCost;
+  p.sm_ctr = p.seg_count + segments;
   p.part_acc = reinterpret_cast<float*>(w + creg);
   p.part_ml = p.part_acc + slots * (int64_t)geo.kvc * geo.G * D;
   p.out = out;

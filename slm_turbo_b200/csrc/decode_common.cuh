@@ -79,6 +79,8 @@ struct SmemHeader {
   ChunkDesc desc[kMaxStages];
   int has_job;
   int merge_ok;
+  int spiece;  // SM-aware piece 2*sm + arrival (-1: none), set at the launch start
+  int pidx;    // this CTA's piece of the partition (set by the producer)
   int abort;  // a consumer warp gave up on a wait: the others skip the merge
   MergeJob job;
 };
@@ -139,6 +141,14 @@ struct DecodeParams {
   float* part_ml;      // [slots][kvc*G][2] (running max in log2 units, sum)
   float* part_acc;     // [slots][kvc*G][D]  (unnormalised output)
   int32_t* seg_count;  // [ngroups*B] arrivals per segment; zero between launches
+  // SM-aware partition (full grids of two CTAs per SM, 8 kv heads per CTA,
+  // one n-tile): the CTA that arrives second on its SM is the slower one
+  // (its warps lose issue slots to the older CTA's), so chunk ranges are
+  // given per (SM, arrival) with weights part_w0 : part_w1.  sm_ctr: one
+  // arrival word per SM + a CTAs-done word; zero between launches.
+  int sm_weighted, num_sms, part_w0, part_w1;
+  int seg_cost;  // weighted partition: a segment start costs seg_cost/8 chunks
+  int32_t* sm_ctr;
   int32_t* err;
   // fused append (paged layout): one new token per sequence at position
   // len-1, row (seq, kv head) at new_k/new_v + seq*new_seq_stride + head*D,
@@ -180,5 +190,27 @@ __host__ __device__ inline int64_t cta_of_unit(int64_t t, int64_t T, int64_t NC)
 __host__ __device__ inline int64_t cta_start(int64_t c, int64_t T, int64_t NC) {
   return c * T / NC;
 }
+
+// The chunk partition of one launch: NC pieces over T chunks, uniform
+// (piece c = CTA c) or weighted by SM arrival (piece 2*sm + arrival, weights
+// w0 for the first CTA on an SM and w1 for the second).
+struct Partition {
+  int64_t T, NC;
+  int weighted, w0, w1;
+  __host__ __device__ int64_t start(int64_t c) const {
+    if (!weighted) return cta_start(c, T, NC);
+    const int64_t W = (NC / 2) * (w0 + w1);
+    const int64_t cw = (c >> 1) * (w0 + w1) + ((c & 1) ? w0 : 0);
+    return cw * T / W;
+  }
+  // the piece that owns chunk t (largest c with start(c) <= t)
+  __host__ __device__ int64_t owner(int64_t t) const {
+    if (!weighted) return cta_of_unit(t, T, NC);
+    const int64_t W = (NC / 2) * (w0 + w1);
+    const int64_t K = ((t + 1) * W + T - 1) / T - 1;  // largest cw with cw*T/W <= t
+    int64_t c = 2 * (K / (w0 + w1)) + ((K % (w0 + w1)) >= w0 ? 1 : 0);
+    return c < NC - 1 ? c : NC - 1;
+  }
+};
 
 }  // namespace slmt

@@ -54,6 +54,24 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
   return v;
 }
 
+__device__ __forceinline__ long long warp_incl_scan_ll(long long v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    long long t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+// Cost positions of the weighted partition: a non-empty segment costs SC
+// units for its start and U8 per chunk; chunk t of the segment with ordinal e
+// (among non-empty segments, in (group, sequence) order) sits at its last
+// unit, SC*(e+1) + U8*(t+1) - 1.  SC = 0, U8 = 1 is the plain chunk index.
+__device__ __forceinline__ long long cost_pos(long long t, long long e, int SC, int U8) {
+  return (long long)SC * (e + 1) + (long long)U8 * (t + 1) - 1;
+}
+
 // Wait until the low 16 bits of `word` (published by other CTAs with a
 // fence before their atomic add) reach n; false after limit_ns.
 __device__ __forceinline__ bool spin_until_arrived(const unsigned int* word, unsigned int n,
@@ -98,6 +116,43 @@ __device__ __forceinline__ int seq_len_raw(const DecodeParams& p, int b) {
   if (p.seq_lens) return p.seq_lens[b];
   return p.seq_len_scalar;
 }
+
+// First chunk (global index) whose cost position is >= x (the total chunk
+// count if none): the start of the piece whose cost range begins at x.
+__device__ inline long long chunk_at_cost(const DecodeParams& p, long long x, long long t_seq, int e_seq, int SC, int U8) {
+  const int lane = threadIdx.x & 31;
+  const int B = p.num_seqs;
+  const long long Gc = (long long)SC * e_seq + (long long)U8 * t_seq;  // cost of one kv-head group
+  if (Gc <= 0 || x >= Gc * p.ngroups) return t_seq * p.ngroups;
+  const long long kg = x / Gc;
+  const long long xr = x - kg * Gc;
+  long long cb = 0, ps = 0;  // cost and chunks of the group's sequences before `base`
+  for (int base = 0; base < B; base += 32) {
+    const int b = base + lane;
+    const int n = (b < B) ? nchunks_of(seq_len_of(p, b)) : 0;
+    const long long cst = n > 0 ? (long long)SC + (long long)U8 * n : 0;
+    const long long ci = warp_incl_scan_ll(cst);
+    const int ni = warp_incl_scan(n);
+    const long long ctot = __shfl_sync(0xffffffffu, ci, 31);
+    const int ntot = __shfl_sync(0xffffffffu, ni, 31);
+    if (cb + ctot > xr) {
+      const unsigned m = __ballot_sync(0xffffffffu, cb + ci > xr);
+      const int src = __ffs(m) - 1;
+      const long long cbefore = cb + __shfl_sync(0xffffffffu, ci - cst, src);
+      const long long nbefore = ps + __shfl_sync(0xffffffffu, ni - n, src);
+      const int nb = __shfl_sync(0xffffffffu, n, src);
+      // first chunk j of that sequence with cbefore + SC + U8*(j+1) - 1 >= xr
+      long long j = xr - cbefore - SC + 1 - U8;
+      j = j <= 0 ? 0 : (j + U8 - 1) / U8;
+      if (j > nb) j = nb;
+      return kg * t_seq + nbefore + j;
+    }
+    cb += ctot;
+    ps += ntot;
+  }
+  return (kg + 1) * t_seq;
+}
+
 
 __device__ __forceinline__ int64_t block_entry(const DecodeParams& p, int s, int blk) {
   if (p.bt_i64)
@@ -270,27 +325,55 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
   constexpr int HALF = D / 2;
   const int lane = threadIdx.x & 31;
   const int B = p.num_seqs;
-  const int c = blockIdx.x;
 
-  // Chunks per kv-head group; flag lengths above capacity once per grid.
+  // Chunks (and non-empty sequences) per kv-head group; flag lengths above
+  // capacity once per grid.
   long long t_seq = 0;
+  int e_seq = 0;
   for (int base = 0; base < B; base += 32) {
     const int b = base + lane;
     int n = 0;
     if (b < B) {
       n = nchunks_of(seq_len_of(p, b));
-      if (c == 0 && seq_len_raw(p, b) > p.len_cap) set_err(p, 8u);
+      if (blockIdx.x == 0 && seq_len_raw(p, b) > p.len_cap) set_err(p, 8u);
     }
     t_seq += warp_sum_i(n);
+    e_seq += warp_sum_i(n > 0 ? 1 : 0);
   }
   const long long T = t_seq * p.ngroups;
-  // never more CTAs than chunks, so every working CTA owns at least one
-  const long long nc_eff = T < p.num_ctas ? T : p.num_ctas;
-  const long long t_begin = c < nc_eff ? cta_start(c, T, nc_eff) : 0;
-  const long long t_end = c < nc_eff ? cta_start(c + 1, T, nc_eff) : 0;
+  // SM-aware weighted pieces when the host enabled them and every piece gets
+  // chunks, over cost positions that charge each segment start SC units
+  // (8 per chunk); else piece = CTA index over plain chunk indices, never
+  // more CTAs than chunks, so every working CTA owns at least one
+  const bool use_w = p.sm_weighted && T >= 8LL * p.num_ctas;
+  const long long nc_eff = use_w ? p.num_ctas : (T < p.num_ctas ? T : p.num_ctas);
+  const int SC = use_w ? p.seg_cost : 0;
+  const int U8 = use_w ? 8 : 1;
+  const long long Ctot = (long long)SC * e_seq * p.ngroups + (long long)U8 * T;
+  // (weights re-read from the kernel parameters at each use: no registers held)
+  auto part = [&]() { return Partition{Ctot, nc_eff, use_w ? 1 : 0, p.part_w0, p.part_w1}; };
+  int c = (int)blockIdx.x;
+  if (use_w) {
+    c = hdr->spiece;
+    if (c < 0) {  // placement other than two CTAs per SM: this CTA works on nothing
+      if (lane == 0) set_err(p, 16u);
+      c = (int)nc_eff;
+    }
+  }
+  if (lane == 0) hdr->pidx = c;  // read by the consumers after their main loop
+  long long t_begin = 0, t_end = 0;
+  if (c < nc_eff) {
+    if (use_w) {
+      t_begin = chunk_at_cost(p, part().start(c), t_seq, e_seq, SC, U8);
+      t_end = chunk_at_cost(p, part().start(c + 1), t_seq, e_seq, SC, U8);
+    } else {
+      t_begin = part().start(c);
+      t_end = part().start(c + 1);
+    }
+  }
 
   // sequences without tokens get zeros (no segment ever writes them)
-  for (int b = c; b < B; b += gridDim.x) {
+  for (int b = (int)blockIdx.x; b < B; b += gridDim.x) {
     if (seq_len_of(p, b) != 0) continue;
     for (int i = lane; i < p.hq * D; i += 32) {
       const int64_t o = (int64_t)b * p.out_seq_stride + (int64_t)(i / D) * p.out_head_stride + i % D;
@@ -311,22 +394,27 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
   if (t_begin < t_end) {
     int kg = (int)(t_begin / t_seq);
     const long long tt = t_begin - (long long)kg * t_seq;
-    // Locate the sequence holding chunk tt of group kg (second pass hits L1).
+    // Locate the sequence holding chunk tt of group kg (second pass hits L1),
+    // and its ordinal among the non-empty segments.
     int s = 0;
     long long ps = 0;
+    long long eord = (long long)kg * e_seq;
     for (int base = 0; base < B; base += 32) {
       const int b = base + lane;
       const int n = (b < B) ? nchunks_of(seq_len_of(p, b)) : 0;
       const int incl = warp_incl_scan(n);
+      const int eincl = warp_incl_scan(n > 0 ? 1 : 0);
       const int tot = __shfl_sync(0xffffffffu, incl, 31);
       if (ps + tot > tt) {
         const unsigned m = __ballot_sync(0xffffffffu, ps + incl > tt);
         const int src = __ffs(m) - 1;
         s = base + src;
         ps += __shfl_sync(0xffffffffu, incl - n, src);
+        eord += __shfl_sync(0xffffffffu, eincl - (n > 0 ? 1 : 0), src);
         break;
       }
       ps += tot;
+      eord += __shfl_sync(0xffffffffu, eincl, 31);
     }
     int chunk = (int)(tt - ps);
     int L = seq_len_of(p, s);
@@ -396,12 +484,15 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
       if (first) {
         // CTAs whose ranges cover this segment (its chunk 0 is global chunk t - chunk)
         const long long p0 = t - chunk;
-        seg_cfirst = (int)cta_of_unit(p0, T, nc_eff);
-        const int c_last = (int)cta_of_unit(p0 + nch - 1, T, nc_eff);
+        seg_cfirst = (int)part().owner(cost_pos(p0, eord, SC, U8));
+        const int c_last = (int)part().owner(cost_pos(p0 + nch - 1, eord, SC, U8));
         seg_ncov = c_last - seg_cfirst + 1;
         // CTAs c_first .. c_last-1 end their ranges inside the segment; c_last
-        // does too when the segment ends exactly where its range ends
-        seg_mergers = seg_ncov - 1 + (cta_start(c_last + 1, T, nc_eff) == p0 + nch ? 1 : 0);
+        // does too when the segment ends exactly where its range ends (the
+        // next chunk, the next segment's first, belongs to a later piece)
+        const long long tn = p0 + nch;
+        seg_mergers = seg_ncov - 1 +
+                      ((tn >= T || part().owner(cost_pos(tn, eord + 1, SC, U8)) > c_last) ? 1 : 0);
       }
       const bool last = (chunk == nch - 1) || (t == t_end - 1);
       const int nvalid = min(kChunkTokens, L - chunk * kChunkTokens);
@@ -647,6 +738,7 @@ __device__ void decode_producer(const DecodeParams& p, SmemHeader* hdr,
         chunk = 0;
         first = true;
         ++seg;
+        ++eord;
         if (pg_mode0) {
           const int ntile = (L + kTileTokens - 1) / kTileTokens;
           pg_base = 0;
@@ -1491,7 +1583,7 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
     __threadfence();
     if (hdr->merge_ok) {
       const int items = kvc * G * (D / 4);
-      const int k = (int)blockIdx.x - job.c_first;
+      const int k = hdr->pidx - job.c_first;
       const int i0 = (int)((int64_t)k * items / job.nmergers);
       const int i1 = (int)((int64_t)(k + 1) * items / job.nmergers);
       merge_segment<D, KVC>(p, job, i0, i1, reinterpret_cast<float*>(const_cast<uint8_t*>(stg)),
@@ -1540,6 +1632,17 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
     mbar_init(&hdr->appended, KVC);
     hdr->has_job = 0;
     hdr->abort = 0;
+    int sp = -1;
+    if (p.sm_weighted) {
+      unsigned smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      if ((int)smid < p.num_sms) {
+        const int r = atomicAdd(p.sm_ctr + smid, 1);
+        if (r < 2) sp = 2 * (int)smid + r;
+      }
+    }
+    hdr->spiece = sp;
+    hdr->pidx = (int)blockIdx.x;
     fence_mbar_init();
   }
   __syncthreads();
@@ -1547,6 +1650,16 @@ __global__ void __launch_bounds__(cta_threads(KVC), ctas_per_sm(KVC, NT))
     decode_producer<D, LAYOUT, APPEND>(p, hdr, qbuf, rbuf, stg);
   else
     decode_consumer<D, NT, LAYOUT, KVC, PK, APPEND, SWZ>(p, hdr, qbuf, rbuf, stg);
+  if (p.sm_weighted) {
+    // the last CTA to finish zeroes the SM arrival words for the next launch
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int done = atomicAdd(p.sm_ctr + p.num_sms, 1);
+      if (done == (int)gridDim.x - 1)
+        for (int i = 0; i <= p.num_sms; ++i) p.sm_ctr[i] = 0;
+    }
+  }
 }
 
 }  // namespace slmt
