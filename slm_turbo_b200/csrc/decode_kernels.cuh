@@ -1366,6 +1366,40 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const int n = PK ? (g & 3) : nt * 8 + g;  // PK: columns 4..7 repeat heads 0..3
+          if constexpr (LAYOUT != LAYOUT_PER_CHANNEL && (D / 8) % 4 == 0) {
+            if (!p.q_bf16) {
+              // fp16 q, whole K words (D 64 / 128): k-slots 0 and 2 are the
+              // adjacent dims 2b, 2b+1, slots 1 and 3 are 2b+4, 2b+5 (b =
+              // this k-step's K byte): two 4-byte reads give the fragment
+              // words by byte permutes, the sums take the same order as below
+              uint32_t fa = 0u, fb = 0u;
+              if (n < G) {
+                const int b = kword_byte<D>(r, s >> 1) + (s & 1);
+                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(qh + n * D + 2 * b);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(qh + n * D + 2 * b + 4);
+                fa = __byte_perm(w0, w1, 0x5410);
+                fb = __byte_perm(w0, w1, 0x7632);
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w0));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w1));
+                part[nt] += f0.x;
+                part[nt] += f1.x;
+                part[nt] += f0.y;
+                part[nt] += f1.y;
+                bpart[nt] += f0.x * 1024.f;
+                bpart[nt] += f1.x * 1024.f;
+                bpart[nt] += f0.y * 64.f;
+                bpart[nt] += f1.y * 64.f;
+              }
+              if (s & 1) {
+                w.qf[nt][s >> 1].z = fa;
+                w.qf[nt][s >> 1].w = fb;
+              } else {
+                w.qf[nt][s >> 1].x = fa;
+                w.qf[nt][s >> 1].y = fb;
+              }
+              continue;
+            }
+          }
           float x[4] = {0.f, 0.f, 0.f, 0.f};
           if (n < G) {
 #pragma unroll
