@@ -10,8 +10,15 @@ namespace slmt {
 // A CTA has one consumer warp per kv head of its group (KVC of them, 1..8)
 // and one producer warp.
 __host__ __device__ constexpr int cta_threads(int kvc) { return (kvc + 1) * 32; }
+// Resident CTAs per SM the kernels are built for: about 18 warps per SM with
+// one n-tile (96 registers: a sub-partition holds up to 5 such warps), but 16
+// (128 registers) with 1 or 2 kv heads per CTA, whose many small CTAs spill at
+// 96; about 9 warps with two n-tiles.
+__host__ __device__ constexpr int warps_per_sm_target(int kvc, int nt) {
+  return nt == 1 ? (kvc <= 2 ? 16 : 18) : 9;
+}
 __host__ __device__ constexpr int ctas_per_sm(int kvc, int nt) {
-  return ((nt == 1) ? 18 : 9) / (kvc + 1) > 0 ? ((nt == 1) ? 18 : 9) / (kvc + 1) : 1;
+  return warps_per_sm_target(kvc, nt) / (kvc + 1) > 0 ? warps_per_sm_target(kvc, nt) / (kvc + 1) : 1;
 }
 constexpr int kMaxStages = 8;
 constexpr int kMaxEnds = 8;  // segment ends per range whose new token is quantized at the start
