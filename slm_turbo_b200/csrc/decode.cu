@@ -314,6 +314,8 @@ int launch_decode(DecodeParams& p, int layout, int D, const Geometry& geo,
   p.out_dtype = out_dtype;
   p.out_seq_stride = out_seq_stride;
   p.out_head_stride = out_head_stride;
+  p.out_pair = reinterpret_cast<uintptr_t>(out) % (out_dtype == 2 ? 8 : 4) == 0 && out_seq_stride % 2 == 0 &&
+               out_head_stride % 2 == 0;
   p.wait_limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
   p.debug_stall = g_debug_stall.load(std::memory_order_relaxed);
 

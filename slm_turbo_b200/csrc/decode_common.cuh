@@ -169,6 +169,7 @@ struct DecodeParams {
   // output element (seq, head, d) at out + seq*out_seq_stride + head*out_head_stride + d
   void* out;
   int out_dtype;  // 0 f16, 1 bf16, 2 f32
+  int out_pair;   // base and strides let adjacent (even, odd) dims be stored as one pair
   int64_t out_seq_stride, out_head_stride;
 };
 

@@ -1560,8 +1560,22 @@ __device__ void decode_consumer(const DecodeParams& p, SmemHeader* hdr,
                 o1 = __half2float(vsc[d0 + 1]) * (o1 - __half2float(vze[d0 + 1]) * lsum);
               }
               if (direct) {
-                store_out(p, obase + 2 * mt, o0 * inv);
-                store_out(p, obase + 2 * mt + 1, o1 * inv);
+                // the two values are adjacent dims: one paired store when the
+                // host found the output's element offsets even
+                if (p.out_pair) {
+                  if (p.out_dtype == 2)
+                    *reinterpret_cast<float2*>(reinterpret_cast<float*>(p.out) + obase + 2 * mt) =
+                        make_float2(o0 * inv, o1 * inv);
+                  else if (p.out_dtype == 1)
+                    *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(p.out) + obase + 2 * mt) =
+                        __floats2bfloat162_rn(o0 * inv, o1 * inv);
+                  else
+                    *reinterpret_cast<uint32_t*>(reinterpret_cast<uint16_t*>(p.out) + obase + 2 * mt) =
+                        pack_half2(o0 * inv, o1 * inv);
+                } else {
+                  store_out(p, obase + 2 * mt, o0 * inv);
+                  store_out(p, obase + 2 * mt + 1, o1 * inv);
+                }
               } else {
                 reinterpret_cast<float2*>(dst)[mt] = make_float2(o0, o1);
               }
