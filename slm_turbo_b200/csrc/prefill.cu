@@ -184,6 +184,13 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
       reinterpret_cast<uint16_t*>(&rul[0][0])[i] = src[(int64_t)kvh * D + (i % D)];
     }
   }
+  // Per-channel rulers are folded out of the chunk: the chunk holds the raw
+  // codes as exact fp16, the key scale is multiplied into q (the key zero
+  // adds the same term to every score of a row, which the softmax drops),
+  // and the value scale and zero are applied once to the normalised output.
+  constexpr bool kPC = (LAYOUT == PF_PER_CHANNEL);
+  const bool pcq = kPC && p.use_quant && S > 0;
+  if (kPC) __syncthreads();  // rul is read by the q load below
 
   // ---- Q A-fragments of rows mw+g and mw+g+8 (zeros past M) ----
   uint32_t qa[KS][4];
@@ -197,7 +204,18 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
         uint32_t w = 0u;
         if (row < M) {
           const int64_t qo = (int64_t)(row0 + row) * p.q_row_stride + (int64_t)h * p.q_head_stride + col;
-          if (p.q_bf16) {
+          if (kPC && pcq) {  // fp16(q * key scale)
+            float2 qf;
+            if (p.q_bf16) {
+              const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(p.q) + qo;
+              qf = make_float2(__bfloat162float(qb[0]), __bfloat162float(qb[1]));
+            } else {
+              qf = __half22float2(*reinterpret_cast<const __half2*>(reinterpret_cast<const __half*>(p.q) + qo));
+            }
+            const float2 sc = __half22float2(*reinterpret_cast<const __half2*>(&rul[0][col]));
+            const __half2 hv = __floats2half2_rn(qf.x * sc.x, qf.y * sc.y);
+            w = *reinterpret_cast<const uint32_t*>(&hv);
+          } else if (p.q_bf16) {
             const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(p.q) + qo;
             const __half2 hv = __floats2half2_rn(__bfloat162float(qb[0]), __bfloat162float(qb[1]));
             w = *reinterpret_cast<const uint32_t*>(&hv);
@@ -283,28 +301,39 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
       const int d0 = 8 * wr;
       const uint32_t word =
           *reinterpret_cast<const uint32_t*>(src + isv * kPfTokens * (D / 2) + tok * (D / 2) + 4 * wr);
-      float vals[8];
-      if (LAYOUT == PF_PER_CHANNEL) {
-        const __half* sc = rul[isv ? 2 : 0];
-        const __half* zp = rul[isv ? 3 : 1];
+      if (kPC) {
+        // codes as exact fp16: nibble | 0x6400 is 1024 + c, minus 1024.
+        // a/b/c/d hold dims (0,4)/(1,5)/(2,6)/(3,7) in their (low, high) halves.
+        const uint32_t a = (word & 0x000F000Fu) | 0x64006400u;
+        const uint32_t b = ((word >> 4) & 0x000F000Fu) | 0x64006400u;
+        const uint32_t c = ((word >> 8) & 0x000F000Fu) | 0x64006400u;
+        const uint32_t d = ((word >> 12) & 0x000F000Fu) | 0x64006400u;
+        const uint32_t x[4] = {__byte_perm(a, b, 0x5410), __byte_perm(c, d, 0x5410), __byte_perm(a, b, 0x7632),
+                               __byte_perm(c, d, 0x7632)};
+        const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6400u));
+        uint32_t y[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float c = (float)((word >> (4 * e)) & 15u);
-          vals[e] = p.use_quant ? (c - __half2float(zp[d0 + e])) * __half2float(sc[d0 + e]) : c;
+        for (int e = 0; e < 4; ++e) {
+          const __half2 hv = __hsub2(*reinterpret_cast<const __half2*>(&x[e]), bias);
+          y[e] = *reinterpret_cast<const uint32_t*>(&hv);
         }
-      } else {
+        *reinterpret_cast<uint4*>((isv ? vsh : ksh) + tok * LD + d0) = make_uint4(y[0], y[1], y[2], y[3]);
+        continue;
+      }
+      {
+        float vals[8];
         const uint2 ru = *reinterpret_cast<const uint2*>(src + 2 * kPfTokens * (D / 2) + tok * 8);
         const uint32_t rp = isv ? ru.y : ru.x;  // (min, step)
         const float2 mn_st = __half22float2(*reinterpret_cast<const __half2*>(&rp));
 #pragma unroll
         for (int e = 0; e < 8; ++e) vals[e] = fmaf((float)((word >> (4 * e)) & 15u), mn_st.y, mn_st.x);
-      }
-      __half2 hv[4];
+        __half2 hv[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(vals[2 * e], vals[2 * e + 1]);
-      *reinterpret_cast<uint4*>((isv ? vsh : ksh) + tok * LD + d0) =
-          make_uint4(*reinterpret_cast<const uint32_t*>(&hv[0]), *reinterpret_cast<const uint32_t*>(&hv[1]),
-                     *reinterpret_cast<const uint32_t*>(&hv[2]), *reinterpret_cast<const uint32_t*>(&hv[3]));
+        for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(vals[2 * e], vals[2 * e + 1]);
+        *reinterpret_cast<uint4*>((isv ? vsh : ksh) + tok * LD + d0) =
+            make_uint4(*reinterpret_cast<const uint32_t*>(&hv[0]), *reinterpret_cast<const uint32_t*>(&hv[1]),
+                       *reinterpret_cast<const uint32_t*>(&hv[2]), *reinterpret_cast<const uint32_t*>(&hv[3]));
+      }
     }
     __syncthreads();
 
@@ -366,10 +395,18 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
       for (int n = 0; n < NTS; ++n) {
         const float p0 = exp2_approx(s[n][0] - msafe[0]), p1 = exp2_approx(s[n][1] - msafe[0]);
         const float p2 = exp2_approx(s[n][2] - msafe[1]), p3 = exp2_approx(s[n][3] - msafe[1]);
-        lrow[0] += p0 + p1;
-        lrow[1] += p2 + p3;
         pa[n][0] = pack_half2(p0, p1);
         pa[n][1] = pack_half2(p2, p3);
+        if (kPC) {  // the sum of the fp16 weights the tensor core multiplies: o / l is then
+                    // a convex combination of the codes, and (o / l - zero) * scale exact
+          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&pa[n][0]));
+          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&pa[n][1]));
+          lrow[0] += f0.x + f0.y;
+          lrow[1] += f1.x + f1.y;
+        } else {
+          lrow[0] += p0 + p1;
+          lrow[1] += p2 + p3;
+        }
       }
       // ---- 4. O += P V ----
 #pragma unroll
@@ -401,8 +438,16 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
     const int64_t base = (int64_t)(row0 + row) * p.out_row_stride + (int64_t)h * p.out_head_stride;
 #pragma unroll
     for (int n = 0; n < NTO; ++n) {
-      store_elem(p, base + 8 * n + 2 * r, o[n][2 * e] * inv);
-      store_elem(p, base + 8 * n + 2 * r + 1, o[n][2 * e + 1] * inv);
+      float v0 = o[n][2 * e] * inv, v1 = o[n][2 * e + 1] * inv;
+      if (kPC && pcq && l > 0.f) {
+        const int dd = 8 * n + 2 * r;
+        const float2 vs = __half22float2(*reinterpret_cast<const __half2*>(&rul[2][dd]));
+        const float2 vz = __half22float2(*reinterpret_cast<const __half2*>(&rul[3][dd]));
+        v0 = (v0 - vz.x) * vs.x;
+        v1 = (v1 - vz.y) * vs.y;
+      }
+      store_elem(p, base + 8 * n + 2 * r, v0);
+      store_elem(p, base + 8 * n + 2 * r + 1, v1);
     }
   }
 }
