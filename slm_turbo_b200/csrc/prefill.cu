@@ -301,39 +301,34 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
       const int d0 = 8 * wr;
       const uint32_t word =
           *reinterpret_cast<const uint32_t*>(src + isv * kPfTokens * (D / 2) + tok * (D / 2) + 4 * wr);
+      // codes as exact fp16: nibble | 0x6400 is 1024 + c, minus 1024.
+      // a/b/c/d hold dims (0,4)/(1,5)/(2,6)/(3,7) in their (low, high) halves.
+      const uint32_t a = (word & 0x000F000Fu) | 0x64006400u;
+      const uint32_t b = ((word >> 4) & 0x000F000Fu) | 0x64006400u;
+      const uint32_t c = ((word >> 8) & 0x000F000Fu) | 0x64006400u;
+      const uint32_t d = ((word >> 12) & 0x000F000Fu) | 0x64006400u;
+      const uint32_t x[4] = {__byte_perm(a, b, 0x5410), __byte_perm(c, d, 0x5410), __byte_perm(a, b, 0x7632),
+                             __byte_perm(c, d, 0x7632)};
+      const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6400u));
+      uint32_t y[4];
       if (kPC) {
-        // codes as exact fp16: nibble | 0x6400 is 1024 + c, minus 1024.
-        // a/b/c/d hold dims (0,4)/(1,5)/(2,6)/(3,7) in their (low, high) halves.
-        const uint32_t a = (word & 0x000F000Fu) | 0x64006400u;
-        const uint32_t b = ((word >> 4) & 0x000F000Fu) | 0x64006400u;
-        const uint32_t c = ((word >> 8) & 0x000F000Fu) | 0x64006400u;
-        const uint32_t d = ((word >> 12) & 0x000F000Fu) | 0x64006400u;
-        const uint32_t x[4] = {__byte_perm(a, b, 0x5410), __byte_perm(c, d, 0x5410), __byte_perm(a, b, 0x7632),
-                               __byte_perm(c, d, 0x7632)};
-        const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6400u));
-        uint32_t y[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const __half2 hv = __hsub2(*reinterpret_cast<const __half2*>(&x[e]), bias);
           y[e] = *reinterpret_cast<const uint32_t*>(&hv);
         }
-        *reinterpret_cast<uint4*>((isv ? vsh : ksh) + tok * LD + d0) = make_uint4(y[0], y[1], y[2], y[3]);
-        continue;
-      }
-      {
-        float vals[8];
+      } else {  // c * step + min, one fp16 rounding (fused multiply-add on half pairs)
         const uint2 ru = *reinterpret_cast<const uint2*>(src + 2 * kPfTokens * (D / 2) + tok * 8);
         const uint32_t rp = isv ? ru.y : ru.x;  // (min, step)
-        const float2 mn_st = __half22float2(*reinterpret_cast<const __half2*>(&rp));
+        const __half2 ms = *reinterpret_cast<const __half2*>(&rp);
+        const __half2 mn = __low2half2(ms), st = __high2half2(ms);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) vals[e] = fmaf((float)((word >> (4 * e)) & 15u), mn_st.y, mn_st.x);
-        __half2 hv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(vals[2 * e], vals[2 * e + 1]);
-        *reinterpret_cast<uint4*>((isv ? vsh : ksh) + tok * LD + d0) =
-            make_uint4(*reinterpret_cast<const uint32_t*>(&hv[0]), *reinterpret_cast<const uint32_t*>(&hv[1]),
-                       *reinterpret_cast<const uint32_t*>(&hv[2]), *reinterpret_cast<const uint32_t*>(&hv[3]));
+        for (int e = 0; e < 4; ++e) {
+          const __half2 hv = __hfma2(__hsub2(*reinterpret_cast<const __half2*>(&x[e]), bias), st, mn);
+          y[e] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
       }
+      *reinterpret_cast<uint4*>((isv ? vsh : ksh) + tok * LD + d0) = make_uint4(y[0], y[1], y[2], y[3]);
     }
     __syncthreads();
 
