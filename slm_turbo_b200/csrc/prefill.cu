@@ -34,6 +34,7 @@
 #include <cuda_fp16.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "internal.h"
 #include "ptx.cuh"
@@ -352,19 +353,29 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
       }
       // ---- 3. mask, online softmax (log2 domain) ----
       float mx[2] = {mrow[0], mrow[1]};
+      // the mask only where some row of the warp does not see the whole
+      // chunk (the causal diagonal, the sequence end); warp-uniform
+      auto scale_scores = [&](auto masked) {
 #pragma unroll
-      for (int n = 0; n < NTS; ++n) {
+        for (int n = 0; n < NTS; ++n) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = mw + g + ((i & 2) ? 8 : 0);
-          const int tok = t0 + 8 * n + 2 * r + (i & 1);
-          const int lim = p.causal ? min(S, off + row + 1) : S;
-          float v = s[n][i] * p.scale_log2;
-          v = tok < lim ? v : -INFINITY;
-          s[n][i] = v;
-          mx[i >> 1] = fmaxf(mx[i >> 1], v);
+          for (int i = 0; i < 4; ++i) {
+            float v = s[n][i] * p.scale_log2;
+            if constexpr (decltype(masked)::value) {
+              const int row = mw + g + ((i & 2) ? 8 : 0);
+              const int tok = t0 + 8 * n + 2 * r + (i & 1);
+              const int lim = p.causal ? min(S, off + row + 1) : S;
+              v = tok < lim ? v : -INFINITY;
+            }
+            s[n][i] = v;
+            mx[i >> 1] = fmaxf(mx[i >> 1], v);
+          }
         }
-      }
+      };
+      if (t0 + kPfTokens <= (p.causal ? min(S, off + mw + 1) : S))
+        scale_scores(std::false_type{});
+      else
+        scale_scores(std::true_type{});
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 1));
