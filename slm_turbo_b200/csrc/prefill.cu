@@ -138,7 +138,7 @@ __device__ __forceinline__ void pf_cp_async8(uint32_t dst, const void* src) {
 // HPC query heads of one kv group per CTA (4 warps each, rows m0.. m0+63):
 // the dequantized chunk is shared by all of them.
 template <int D, int LAYOUT, int HPC>
-__global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constant__ PrefillParams p) {
+__global__ void __launch_bounds__(128 * HPC, (D <= 80 && HPC == 2) ? 2 : 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   constexpr int NTHR = 128 * HPC;
   constexpr int KS = D / 16;   // k-steps of QK
   constexpr int NTO = D / 8;   // n-tiles of O
@@ -338,17 +338,23 @@ __global__ void __launch_bounds__(128 * HPC) prefill_kernel(const __grid_constan
       float s[NTS][4];
 #pragma unroll
       for (int n = 0; n < NTS; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+      // k-steps outer, the 8 token tiles inner: consecutive tensor-core ops
+      // update different accumulators instead of one dependent chain
 #pragma unroll
-      for (int n = 0; n < NTS; ++n) {
+      for (int ks = 0; ks < KS; ks += 2) {
+        // matrices: (k-step ks, dims 0-7), (ks, 8-15), (ks+1, 0-7), (ks+1, 8-15) of tokens 8n..8n+7
+        const int mi = lane >> 3, ri = lane & 7;
+        const int kk = (ks + (mi >> 1) < KS) ? ks + (mi >> 1) : ks;
+        uint32_t bb[NTS][4];
 #pragma unroll
-        for (int ks = 0; ks < KS; ks += 2) {
-          // matrices: (k-step ks, dims 0-7), (ks, 8-15), (ks+1, 0-7), (ks+1, 8-15) of tokens 8n..8n+7
-          const int mi = lane >> 3, ri = lane & 7;
-          const int kk = (ks + (mi >> 1) < KS) ? ks + (mi >> 1) : ks;
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(b0, b1, b2, b3, ksh + (8 * n + ri) * LD + 16 * kk + 8 * (mi & 1));
-          mma_16816(s[n], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
-          if (ks + 1 < KS) mma_16816(s[n], qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], b2, b3);
+        for (int n = 0; n < NTS; ++n)
+          ldsm_x4(bb[n][0], bb[n][1], bb[n][2], bb[n][3], ksh + (8 * n + ri) * LD + 16 * kk + 8 * (mi & 1));
+#pragma unroll
+        for (int n = 0; n < NTS; ++n) mma_16816(s[n], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], bb[n][0], bb[n][1]);
+        if (ks + 1 < KS) {
+#pragma unroll
+          for (int n = 0; n < NTS; ++n)
+            mma_16816(s[n], qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], bb[n][2], bb[n][3]);
         }
       }
       // ---- 3. mask, online softmax (log2 domain) ----
