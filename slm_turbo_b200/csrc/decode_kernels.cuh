@@ -980,74 +980,77 @@ __device__ __forceinline__ void consume_chunk(const DecodeParams& p, WarpState<D
   constexpr int NA = PK ? 1 : 2;     // score tiles held per thread
   const int at = PK ? (r >> 1) : 0;  // PK: the tile of this thread's columns
 
-  // ---- QK on biased codes, tile by tile (one accumulator chain per tile:
-  // a second chain per tile costs registers the kernel does not have) ----
+  // ---- QK on biased codes: both tiles' codes loaded, then their two
+  // accumulator chains advanced in turn (a second chain per tile would cost
+  // registers the kernel does not have) ----
   float sacc[2][NT][4];
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
-    float c[NT][4];
-    asm volatile("" ::: "memory");  // keep the two tiles' loads from being hoisted together
+  for (int a = 0; a < 2; ++a)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      c[nt][0] = c[nt][2] = -w.qb[nt][0];
-      c[nt][1] = c[nt][3] = -w.qb[nt][1];
+      sacc[a][nt][0] = sacc[a][nt][2] = -w.qb[nt][0];
+      sacc[a][nt][1] = sacc[a][nt][3] = -w.qb[nt][1];
     }
-    uint32_t ka[QW], kb[QW];
+  uint32_t ka[2][QW], kb[2][QW];
+#pragma unroll
+  for (int a = 0; a < 2; ++a) {
     const uint8_t* k0 = krow + a * SV::d16;
     if constexpr (SWZ) {
-      // thread-constant swizzled addresses of bytes [8r, +8) and [32+8r, +8)
-      // (D=128) or [8r, +8) (D=64) of rows tg and tg+8
       uint2 x = lds64(kq0 + a * SV::d16), y = lds64(kq0 + a * SV::d16 + SV::d8);
-      ka[0] = x.x;
-      ka[1] = x.y;
-      kb[0] = y.x;
-      kb[1] = y.y;
+      ka[a][0] = x.x;
+      ka[a][1] = x.y;
+      kb[a][0] = y.x;
+      kb[a][1] = y.y;
       if constexpr (QB == 16) {
         x = lds64(kq1 + a * SV::d16);
         y = lds64(kq1 + a * SV::d16 + SV::d8);
-        ka[2] = x.x;
-        ka[3] = x.y;
-        kb[2] = y.x;
-        kb[3] = y.y;
+        ka[a][2] = x.x;
+        ka[a][3] = x.y;
+        kb[a][2] = y.x;
+        kb[a][3] = y.y;
       }
     } else if constexpr (QB == 16) {
-      load_bytes<8, 8>(k0 + 8 * r, ka);
-      load_bytes<8, 8>(k0 + 32 + 8 * r, ka + 2);
-      load_bytes<8, 8>(k0 + SV::d8 + 8 * r, kb);
-      load_bytes<8, 8>(k0 + SV::d8 + 32 + 8 * r, kb + 2);
+      load_bytes<8, 8>(k0 + 8 * r, ka[a]);
+      load_bytes<8, 8>(k0 + 32 + 8 * r, ka[a] + 2);
+      load_bytes<8, 8>(k0 + SV::d8 + 8 * r, kb[a]);
+      load_bytes<8, 8>(k0 + SV::d8 + 32 + 8 * r, kb[a] + 2);
     } else {
-      load_bytes<QB, QALIGN>(k0 + r * QB, ka);
-      load_bytes<QB, QALIGN>(k0 + SV::d8 + r * QB, kb);
+      load_bytes<QB, QALIGN>(k0 + r * QB, ka[a]);
+      load_bytes<QB, QALIGN>(k0 + SV::d8 + r * QB, kb[a]);
     }
+  }
+  // consecutive tensor-core ops belong to different tiles: independent
 #pragma unroll
-    for (int u = 0; u < QW; ++u) {
-      uint4 qf[NT];  // B-fragments of k-steps 2u (x, y) and 2u+1 (z, w)
+  for (int u = 0; u < QW; ++u) {
+    uint4 qf[NT];  // B-fragments of k-steps 2u (x, y) and 2u+1 (z, w)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) qf[nt] = w.qf[nt][u];
-      if (4 * u + 4 <= QB) {
-        uint32_t a0 = codes_lo_biased(ka[u]), a1 = codes_lo_biased(kb[u]);
-        uint32_t a2 = codes_hi_biased(ka[u]), a3 = codes_hi_biased(kb[u]);
+    for (int nt = 0; nt < NT; ++nt) qf[nt] = w.qf[nt][u];
+    if (4 * u + 4 <= QB) {
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
-        const uint32_t sa = ka[u] >> 8, sb = kb[u] >> 8;
-        a0 = codes_lo_biased(sa);
-        a1 = codes_lo_biased(sb);
-        a2 = codes_hi_biased(sa);
-        a3 = codes_hi_biased(sb);
+      for (int a = 0; a < 2; ++a) {
+        const uint32_t a0 = codes_lo_biased(ka[a][u]), a1 = codes_lo_biased(kb[a][u]);
+        const uint32_t a2 = codes_hi_biased(ka[a][u]), a3 = codes_hi_biased(kb[a][u]);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].z, qf[nt].w);
-      } else {
-        const uint32_t sa = __byte_perm(ka[u], 0u, 0x3120), sb = __byte_perm(kb[u], 0u, 0x3120);
+        for (int nt = 0; nt < NT; ++nt) mma_16816(sacc[a][nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
+      }
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        const uint32_t sa = ka[a][u] >> 8, sb = kb[a][u] >> 8;
         const uint32_t a0 = codes_lo_biased(sa), a1 = codes_lo_biased(sb);
         const uint32_t a2 = codes_hi_biased(sa), a3 = codes_hi_biased(sb);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_16816(c[nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
+        for (int nt = 0; nt < NT; ++nt) mma_16816(sacc[a][nt], a0, a1, a2, a3, qf[nt].z, qf[nt].w);
+      }
+    } else {
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        const uint32_t sa = __byte_perm(ka[a][u], 0u, 0x3120), sb = __byte_perm(kb[a][u], 0u, 0x3120);
+        const uint32_t a0 = codes_lo_biased(sa), a1 = codes_lo_biased(sb);
+        const uint32_t a2 = codes_hi_biased(sa), a3 = codes_hi_biased(sb);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_16816(sacc[a][nt], a0, a1, a2, a3, qf[nt].x, qf[nt].y);
       }
     }
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sacc[a][nt][i] = c[nt][i];
   }
   if constexpr (PK) {
 #pragma unroll
